@@ -1,0 +1,184 @@
+// common.cuh -- shared device/host helpers for the sm_100a NVFP4 library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nvfp4_b200.h"
+
+namespace nvfp4b {
+
+// ------------------------------------------------------------------------------------------------------------
+// Host-side helpers
+// ------------------------------------------------------------------------------------------------------------
+
+// Records the failing cudaError_t for nvfp4b_last_cuda_error() and maps it to NVFP4B_ERR_CUDA.
+int record_cuda_error(cudaError_t e);
+
+// Status of the launch that was just issued (cudaGetLastError), as an NVFP4B status.
+inline int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
+}
+
+// Streaming-multiprocessor count of the current device (cached per device).
+int sm_count();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline size_t scale_bytes(int outer, int K) {
+    const size_t tiles_r = (size_t)((outer + 127) / 128), tiles_c = (size_t)((K / 16 + 3) / 4);
+    return tiles_r * tiles_c * 512;
+}
+
+constexpr float kGscaleNum = 2688.0f;   // 448 (e4m3 max) * 6 (e2m1 max)
+
+// ------------------------------------------------------------------------------------------------------------
+// NVFP4 numerics shared by the quantiser, the fused MoE dispatch and the GEMM epilogues.
+//
+// The target is the reference's numpy quantiser (scripts/nvfp4_ref.py:43-82), bit for bit:
+//   t      = fl64(g * fl64(bamax / 6))                 e4m3 input, float64
+//   stored = nearest e4m3 >= 0 to t, ties to the smaller value, 0 -> byte 0x80, > 448 -> 448
+//   L      = stored > 0 ? fl64(stored / g) : 1
+//   code   = #{ mid in {.25,.75,1.25,1.75,2.5,3.5,5} : mid < fl64(|x| / L) } | (x < 0 ? 8 : 0)
+// The last line is the reference's "nearest e2m1, ties toward the smaller magnitude": every subtraction in its
+// tie test is exact (Sterbenz), so the test reduces to comparing the float64 quotient with the midpoints.
+//
+// Per element the kernels evaluate the quotient in fp32 twice, scaled by (1 - 2^-20) and (1 + 2^-20); the fp32
+// estimate is within 2^-22.9 relative of the float64 quotient, so the float64 quotient lies strictly between the
+// two.  When both round (cvt.rn.satfinite.e2m1x2) to the same code no midpoint lies between them and that code is
+// the reference's; when they differ, the element is recomputed exactly in float64.  The slow path is taken only
+// for elements within ~1e-6 relative of a rounding boundary.
+// ------------------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float gscale_from_amax(float amax) {
+    return __fdiv_rn(kGscaleNum, fmaxf(amax, 1e-9f));
+}
+
+// 2^e as a double, e in the normal range.
+__device__ __forceinline__ double pow2d(int e) {
+    return __longlong_as_double((long long)(e + 1023) << 52);
+}
+
+// Nearest finite non-negative e4m3 value to t >= 0, ties toward the smaller value.  Returns the byte (0x80 for
+// zero) and writes the value.
+__device__ __forceinline__ uint32_t e4m3_encode_ties_low(double t, double* val) {
+    if (!(t > 0.0)) { *val = 0.0; return 0x80u; }
+    if (t >= 448.0) { *val = 448.0; return 0x7Eu; }
+    int e = ilogb(t);
+    const int es = e < -6 ? -6 : e;                 // values below 2^-6 share the subnormal step 2^-9
+    const double step = pow2d(es - 3);
+    const double n = floor(__dmul_rn(t, pow2d(3 - es)));
+    const double lo = __dmul_rn(n, step), hi = __dmul_rn(n + 1.0, step);
+    double v;
+    if (lo == t) v = t;
+    else v = (__dsub_rn(t, lo) <= __dsub_rn(hi, t)) ? lo : hi;
+    *val = v;
+    if (v == 0.0) return 0x80u;
+    if (v < 0.015625) return (uint32_t)__dmul_rn(v, 512.0);             // subnormal: m * 2^-9
+    const int E = ilogb(v);
+    const uint32_t m = (uint32_t)__dmul_rn(__dsub_rn(__dmul_rn(v, pow2d(-E)), 1.0), 8.0);
+    return ((uint32_t)(E + 7) << 3) | m;
+}
+
+// e4m3 byte -> float (0x80 and 0x00 decode to zero; NaN bytes are never produced here).
+__host__ __device__ __forceinline__ float e4m3_to_float(uint32_t b) {
+    const uint32_t e = (b >> 3) & 0xFu, m = b & 7u;
+    float mag;
+    if (e == 0) {
+        mag = (float)m * (1.0f / 512.0f);
+    } else {
+        union { uint32_t u; float f; } p;
+        p.u = (e - 7u + 127u) << 23;
+        mag = (1.0f + (float)m * 0.125f) * p.f;
+    }
+    return (b & 0x80u) ? -mag : mag;
+}
+
+struct BlockParams {
+    uint32_t sf;    // stored e4m3 byte
+    float invL;     // fp32 estimate of 1/L (fast path)
+    double L;       // exact float64 local scale (slow path)
+};
+
+__device__ __forceinline__ BlockParams block_params(float bamax, float g) {
+    BlockParams p;
+    double stored;
+    const double t = __dmul_rn((double)g, __ddiv_rn((double)bamax, 6.0));
+    p.sf = e4m3_encode_ties_low(t, &stored);
+    if (stored > 0.0) {
+        p.L = __ddiv_rn(stored, (double)g);
+        p.invL = __fdiv_rn(g, (float)stored);
+    } else {
+        p.L = 1.0;
+        p.invL = 1.0f;
+    }
+    return p;
+}
+
+// Exact float64 e2m1 code of x / L (the slow path).
+static __device__ __noinline__ uint32_t e2m1_code_exact(float x, double L) {
+    const double y = __ddiv_rn(fabs((double)x), L);
+    const uint32_t c = (uint32_t)(y > 0.25) + (uint32_t)(y > 0.75) + (uint32_t)(y > 1.25) + (uint32_t)(y > 1.75) +
+                       (uint32_t)(y > 2.5) + (uint32_t)(y > 3.5) + (uint32_t)(y > 5.0);
+    return c | (x < 0.0f ? 8u : 0u);
+}
+
+// Four cvt.rn.satfinite.e2m1x2: 8 floats -> 8 codes in one word, element 0 in the lowest nibble.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(float a0, float a1, float a2, float a3,
+                                               float a4, float a5, float a6, float a7) {
+    uint32_t out;
+    asm("{\n\t.reg .b8 q0, q1, q2, q3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q1, %4, %3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q2, %6, %5;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 q3, %8, %7;\n\t"
+        "mov.b32 %0, {q0, q1, q2, q3};\n\t}"
+        : "=r"(out)
+        : "f"(a0), "f"(a1), "f"(a2), "f"(a3), "f"(a4), "f"(a5), "f"(a6), "f"(a7));
+    return out;
+}
+
+// Codes of 8 consecutive elements v[0..7] of a block with parameters p.
+__device__ __forceinline__ uint32_t encode8(const float* v, const BlockParams& p) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        // v * invL + 0: the +0 addend turns -0.0 into +0.0 (the reference gives code 0 for -0.0) while a
+        // non-zero negative product keeps its sign even when it underflows.
+        const float2 q = __ffma2_rn(make_float2(v[i], v[i + 1]), make_float2(p.invL, p.invL), make_float2(0.f, 0.f));
+        const float2 l = __fmul2_rn(q, make_float2(0.99999904632568359375f, 0.99999904632568359375f));
+        const float2 h = __fmul2_rn(q, make_float2(1.00000095367431640625f, 1.00000095367431640625f));
+        lo[i] = l.x; lo[i + 1] = l.y;
+        hi[i] = h.x; hi[i + 1] = h.y;
+    }
+    const uint32_t wl = cvt_e2m1x8(lo[0], lo[1], lo[2], lo[3], lo[4], lo[5], lo[6], lo[7]);
+    uint32_t wh = cvt_e2m1x8(hi[0], hi[1], hi[2], hi[3], hi[4], hi[5], hi[6], hi[7]);
+    uint32_t diff = wl ^ wh;
+    if (__builtin_expect(diff != 0u, 0)) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if ((diff >> (4 * i)) & 0xFu) {
+                const uint32_t c = e2m1_code_exact(v[i], p.L);
+                wh = (wh & ~(0xFu << (4 * i))) | (c << (4 * i));
+            }
+        }
+    }
+    return wh;
+}
+
+// Quantise one 16-element block: returns the scale byte, writes the 8 code bytes as two words.
+__device__ __forceinline__ uint32_t quantize16(const float* v, float g, uint32_t& w0, uint32_t& w1) {
+    float bamax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(v[i]));
+    const BlockParams p = block_params(bamax, g);
+    w0 = encode8(v, p);
+    w1 = encode8(v + 8, p);
+    return p.sf;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+}  // namespace nvfp4b

@@ -1,0 +1,36 @@
+// runtime.cu -- library-wide host helpers: error bookkeeping, device properties, sizes.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace nvfp4b {
+
+static thread_local int t_last_cuda_error = 0;
+
+int record_cuda_error(cudaError_t e) {
+    t_last_cuda_error = (int)e;
+    return NVFP4B_ERR_CUDA;
+}
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+}  // namespace nvfp4b
+
+extern "C" const char* nvfp4b_version(void) { return "nvfp4_b200 0.1 (sm_100a)"; }
+
+extern "C" int nvfp4b_last_cuda_error(void) { return nvfp4b::t_last_cuda_error; }
+
+extern "C" size_t nvfp4b_scale_buffer_bytes(int outer, int K) {
+    if (outer <= 0 || K <= 0) return 0;
+    return nvfp4b::scale_bytes(outer, K);
+}

@@ -1,0 +1,108 @@
+/* nvfp4_b200.h -- C ABI of the B200 (sm_100a) NVFP4 quantised-matmul library (libnvfp4_b200.so).
+ *
+ * Plain pointers, sizes and an opaque stream handle (a cudaStream_t passed as void*; NULL = the legacy default
+ * stream).  Every function that launches work returns an int status: 0 on success, a negative NVFP4B_ERR_* code
+ * otherwise.  No function allocates device memory, synchronises the host, or calls a CUDA API that is illegal
+ * during stream capture, unless its comment says so.  All device buffers are owned by the caller.
+ *
+ * NVFP4 conventions shared by every entry point:
+ *   codes   : e2m1, two per byte, the even-index element in the low nibble                   [rows, K/2] uint8
+ *   scales  : one e4m3 byte per 16-element block along K, stored in the 128x4-tile layout the tensor cores read
+ *             (tile = 128 rows x 4 blocks = 512 bytes, tiles row-major; within a tile the byte of (m, b) is at
+ *             (m%32)*16 + ((m%128)/32)*4 + (b%4)); rows padded to 128 and blocks to 4 with zero bytes.
+ *             Size: nvfp4b_scale_buffer_bytes(rows, K).
+ *   gscale  : fp32 per-tensor global scale in the compressed-tensors convention, 2688 / amax.  Dequantised value
+ *             = e2m1(code) * e4m3(scale) / gscale.
+ * Rounding follows the reference's numpy quantiser (scripts/nvfp4_ref.py:43-82) bit for bit: float64 block
+ * arithmetic, nearest with ties toward the smaller magnitude for both e4m3 and e2m1, an all-zero block stores
+ * scale byte 0x80.
+ */
+#ifndef NVFP4_B200_H
+#define NVFP4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nvfp4b_status {
+    NVFP4B_OK = 0,
+    NVFP4B_ERR_SHAPE = -1,   /* a dimension is out of range or not a multiple the path requires */
+    NVFP4B_ERR_ALIGN = -2,   /* a pointer or row pitch is not 16-byte aligned */
+    NVFP4B_ERR_NULL = -3,    /* a required pointer is NULL */
+    NVFP4B_ERR_CUDA = -4,    /* a CUDA call failed; nvfp4b_last_cuda_error() has the cudaError_t */
+    NVFP4B_ERR_ARCH = -5,    /* the current device is not an sm_100 part */
+    NVFP4B_ERR_TIMEOUT = -6, /* a bounded device-side wait expired (no fault, the context stays usable) */
+    NVFP4B_ERR_ARG = -7      /* an enum/flag argument has an unknown value */
+};
+
+/* Library version string. */
+const char* nvfp4b_version(void);
+/* cudaError_t of the most recent failing CUDA call made by this thread inside the library (0 if none). */
+int nvfp4b_last_cuda_error(void);
+
+/* Bytes of a swizzled scale buffer for a [outer, K] NVFP4 operand.  Same value as the reference's
+ * nvfp4_scale_buffer_bytes (kernels/fp4_gemm.cu:14-19). */
+size_t nvfp4b_scale_buffer_bytes(int outer, int K);
+
+/* ---- activation quantiser (replaces kernels/nvfp4_quant.cu:15-57; adds bf16 input and device amax) ---------- */
+
+/* d_amax[0] = max |x| over n bf16 values (x is bf16 bit patterns, 16-byte aligned).  Zeroes d_amax first (an
+ * async memset on the stream), then one reduction kernel. */
+int nvfp4b_amax_bf16(const void* x, long long n, float* d_amax, void* stream);
+
+/* Quantise x [M, K] (row-major, bf16 bit patterns) to NVFP4.  K % 16 == 0; x, packed and scales 16-byte aligned.
+ * Global scale: if d_amax is NULL the host value `gscale` is used (static scale, the reference contract of
+ * include/nvfp4_quant.h:10-11); otherwise gscale = 2688 / max(d_amax[0], 1e-9) is computed on the device as one
+ * correctly rounded fp32 division (dynamic scale; pair with nvfp4b_amax_bf16 on the same stream).
+ * packed [M, K/2]; scales: nvfp4b_scale_buffer_bytes(M, K) bytes, fully written including the zero padding. */
+int nvfp4b_quantize_bf16(const void* x, int M, int K, float gscale, const float* d_amax,
+                         uint8_t* packed, uint8_t* scales, void* stream);
+
+/* Same as nvfp4b_quantize_bf16 for fp32 input (the reference entry point's input type). */
+int nvfp4b_quantize_f32(const float* x, int M, int K, float gscale, const float* d_amax,
+                        uint8_t* packed, uint8_t* scales, void* stream);
+
+/* Device relayout of logical scales [outer, K/16] into the tile layout (padding zeroed).  Device-side twin of
+ * the reference's host nvfp4_swizzle_scales (kernels/fp4_gemm.cu:21-33). */
+int nvfp4b_swizzle_scales(const uint8_t* logical, uint8_t* swizzled, int outer, int K, void* stream);
+
+/* ---- W4A4 NVFP4 GEMM (replaces the cuBLASLt call in kernels/fp4_gemm.cu:113-162) ----------------------------- */
+
+enum nvfp4b_out_kind {
+    NVFP4B_OUT_BF16_ROWMAJOR = 0, /* D[m*ldd + n] bf16 */
+    NVFP4B_OUT_F32_COLMAJOR = 1,  /* D[m + n*ldd] fp32 (the reference nvfp4_gemm contract, ldd = M) */
+    NVFP4B_OUT_F32_ROWMAJOR = 2   /* D[m*ldd + n] fp32 */
+};
+
+/* D = alpha * A @ B^T with A = activations [M, K] NVFP4 and B = weights [N, K] NVFP4 (both K-major codes plus
+ * tile-layout scales), fp32 accumulation on the tensor cores (tcgen05 kind::mxf4nvf4, e4m3 scales per 16).
+ * alpha = a_dequant * b_dequant where each dequant multiplier is 1/gscale; if d_a_amax is not NULL the activation
+ * multiplier is instead 1 / (2688 / max(d_a_amax[0], 1e-9)) computed on the device (dynamic activation scale),
+ * i.e. alpha = b_dequant / gscale(amax).  K % 32 == 0 (16-byte rows), pointers 16-byte aligned, ldd >= row length.
+ * Any M, N >= 1. */
+int nvfp4b_gemm(const uint8_t* a, const uint8_t* a_scales, float a_dequant, const float* d_a_amax,
+                const uint8_t* b, const uint8_t* b_scales, float b_dequant,
+                int M, int N, int K, void* d, int out_kind, long long ldd, void* stream);
+
+/* Reads the library's device-side error word (set by a kernel whose bounded wait expired, see
+ * NVFP4B_ERR_TIMEOUT) and optionally clears it.  Synchronous (cudaMemcpyFromSymbol): not for use during capture.
+ * Returns 0 if no kernel reported an error. */
+int nvfp4b_read_device_error(int reset);
+
+/* ---- W4A16 (replaces fp4_gemv / w4a16_gemm, kernels/fp4_gemm.cu:45-111) ----------------------------------- */
+
+/* out[M, N] (fp32 row-major) = x16[M, K] (fp16 row-major) @ dequant(W[N, K])^T with raw, unswizzled weight codes
+ * wp [N, K/2] and e4m3 scales ws [N, K/16]; dequant = code * e4m3 / w_gscale.  K % 16 == 0; any M (the
+ * reference's kernel is limited to M <= 16).  16-byte aligned operands with K % 32 == 0 take the vectorised path,
+ * anything else a byte-granular one. */
+int nvfp4b_w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16,
+                      int M, int N, int K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_B200_H */

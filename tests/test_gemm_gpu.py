@@ -1,0 +1,124 @@
+"""W4A4 NVFP4 GEMM (tcgen05 kind::mxf4nvf4) on the GPU vs the float64 dequant-matmul oracle.
+
+Gates: the reference's own GEMM gate (tests/test_fp4_gemm.cu:61-77) on its generator's fixtures, and the
+elementwise W4A4 bar |Y - Yref| <= 1e-2 |Yref| + 1e-3 max|Yref| (max-norm rel <= 1e-2) on seeded bf16 inputs."""
+import numpy as np
+import pytest
+import torch
+
+import native
+import nvfp4_oracle as orc
+from gpu_util import bf16_to_dev, gate_fp4_gemm, gate_w4a4, require_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("tag", ["default", "ragged"])
+def test_reference_generator_cases_colmajor(golden, tag):
+    """tests/test_fp4_gemm.cu flow: host-swizzled scales, nvfp4_gemm -> fp32 column-major D (ld = M)."""
+    p = require_gpu()
+    g = golden("gemm_cases.npz")
+    M, N, K = [int(v) for v in g[f"{tag}__dims"]]
+    ag, bg = float(g[f"{tag}__ag"]), float(g[f"{tag}__bg"])
+    A, B = _dev(g[f"{tag}__a_packed"]), _dev(g[f"{tag}__b_packed"])
+    As = _dev(orc.swizzle_scales(g[f"{tag}__a_sf"], M, K))
+    Bs = _dev(orc.swizzle_scales(g[f"{tag}__b_sf"], N, K))
+    D = torch.full((N, M), float("nan"), dtype=torch.float32, device="cuda")
+    rc = p.nvfp4_gemm(D, A, As, ag, B, Bs, bg, M, N, K)
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert p.read_device_error() == 0
+    got = D.cpu().numpy().T          # column-major [M, N]
+    ok, msg = gate_fp4_gemm(got, g[f"{tag}__y_ref"])
+    assert ok, msg
+
+
+def _quantized_operands(M, N, K, seed):
+    xb = orc.synth_bf16((M, K), 1.0, seed=seed)
+    wb = orc.synth_bf16((N, K), 0.02, seed=seed + 1)
+    gx = orc.global_scale_from_amax(native.amax_bf16(xb))
+    gw = orc.global_scale_from_amax(native.amax_bf16(wb))
+    px, sx = native.quantize_bf16(xb, gx)
+    pw, sw = native.quantize_bf16(wb, gw)
+    return xb, wb, (px, sx, gx), (pw, sw, gw)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 2048, 2048),                 # cfg0
+                                   (128, 2816, 2816), (256, 8448, 2816), (128, 14336, 4096),   # cfg2 (reduced M)
+                                   (1, 256, 64), (130, 200, 192), (77, 136, 96), (300, 384, 2048)])
+def test_gemm_bf16_vs_dequant_oracle(M, N, K):
+    p = require_gpu()
+    _, _, (px, sx, gx), (pw, sw, gw) = _quantized_operands(M, N, K, seed=M + N + K)
+    A, As = _dev(px), _dev(orc.swizzle_scales(sx, M, K))
+    B, Bs = _dev(pw), _dev(orc.swizzle_scales(sw, N, K))
+    Y = p.gemm(A, As, 1.0 / float(gx), B, Bs, 1.0 / float(gw))
+    torch.cuda.synchronize()
+    assert p.read_device_error() == 0
+    ref = orc.gemm_dequant_ref(px, sx, gx, pw, sw, gw)
+    ok, msg = gate_w4a4(Y.float().cpu().numpy(), ref)
+    assert ok, msg
+
+
+def test_gemm_fp32_rowmajor_and_dynamic_alpha():
+    """fp32 row-major output; activation dequant taken from a device amax (the dynamic-scale pipeline)."""
+    p = require_gpu()
+    M, N, K = 256, 384, 1024
+    xb, wb, (px, sx, gx), (pw, sw, gw) = _quantized_operands(M, N, K, seed=5)
+    x = bf16_to_dev(xb)
+    amax = p.amax(x)
+    xq, xs = p.quantize(x, amax_dev=amax)
+    B, Bs = _dev(pw), _dev(orc.swizzle_scales(sw, N, K))
+    Y = p.gemm(xq, xs, 0.0, B, Bs, 1.0 / float(gw), out_kind=p.OUT_F32_ROWMAJOR, a_amax=amax)
+    torch.cuda.synchronize()
+    ref = orc.gemm_dequant_ref(px, sx, gx, pw, sw, gw)
+    ok, msg = gate_w4a4(Y.cpu().numpy(), ref)
+    assert ok, msg
+
+
+def test_gemm_full_size_cfg2_sampled_rows():
+    """cfg2 at M=4096, (K, N) = (4096, 14336): full-size launch, oracle on 96 sampled rows."""
+    p = require_gpu()
+    M, N, K = 4096, 14336, 4096
+    rng = np.random.default_rng(0)
+    xb = orc.synth_bf16((M, K), 1.0, seed=41)
+    wb = orc.synth_bf16((N, K), 0.02, seed=42)
+    x, w = bf16_to_dev(xb), bf16_to_dev(wb)
+    gx = orc.global_scale_from_amax(native.amax_bf16(xb))
+    gw = orc.global_scale_from_amax(native.amax_bf16(wb))
+    xq, xs = p.quantize(x, gscale=float(gx))
+    wq, ws = p.quantize(w, gscale=float(gw))
+    Y = p.gemm(xq, xs, 1.0 / float(gx), wq, ws, 1.0 / float(gw))
+    torch.cuda.synchronize()
+    assert p.read_device_error() == 0
+    rows = np.sort(rng.choice(M, 96, replace=False))
+    px, sx = native.quantize_bf16(xb[rows], gx)
+    pw, sw = native.quantize_bf16(wb, gw)
+    ref = orc.gemm_dequant_ref(px, sx, gx, pw, sw, gw)
+    ok, msg = gate_w4a4(Y[torch.from_numpy(rows).cuda()].float().cpu().numpy(), ref)
+    assert ok, msg
+
+
+def test_gemm_matches_reference_cublaslt_when_built():
+    """Same operands through the reference's own nvfp4_gemm (cuBLASLt), built from its sources in oracle/_ref."""
+    p = require_gpu()
+    ref_lib = native.ref_lib()
+    if ref_lib is None:
+        pytest.skip("oracle/_ref not built")
+    M, N, K = 256, 512, 1024
+    _, _, (px, sx, gx), (pw, sw, gw) = _quantized_operands(M, N, K, seed=17)
+    A, As = _dev(px), _dev(orc.swizzle_scales(sx, M, K))
+    B, Bs = _dev(pw), _dev(orc.swizzle_scales(sw, N, K))
+    D_ours = torch.empty((N, M), dtype=torch.float32, device="cuda")
+    D_ref = torch.empty((N, M), dtype=torch.float32, device="cuda")
+    assert p.nvfp4_gemm(D_ours, A, As, 1.0 / float(gx), B, Bs, 1.0 / float(gw), M, N, K) == 0
+    rc = ref_lib.ref_nvfp4_gemm(D_ref.data_ptr(), A.data_ptr(), As.data_ptr(), 1.0 / float(gx), B.data_ptr(),
+                                Bs.data_ptr(), 1.0 / float(gw), M, N, K, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    if rc != 0:
+        pytest.skip(f"reference cuBLASLt nvfp4_gemm returned {rc} on this box")
+    ok, msg = gate_fp4_gemm(D_ours.cpu().numpy(), D_ref.cpu().numpy())
+    assert ok, msg
