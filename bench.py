@@ -1,0 +1,421 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 NVFP4 path; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload quant|gemm|moe] [--impl ours|reference]
+
+Workloads (synthetic seeded inputs with the configs' shapes and distributions):
+  quant (default)  cfg1 at its largest size: bf16 [8192, 2816] ~ N(0,1) with 0.1% x50 outliers.  One step = device
+                   global amax + NVFP4 quantise (codes, tile-layout e4m3 scales, fp32 amax).  Metric GB/s of
+                   algorithmic bytes T*K*(2 + 1/2 + 1/16) + 4.
+  gemm             cfg2 at its largest size: M=8192, K=4096, N=14336, NVFP4 A and W resident, bf16 out with the
+                   fused global-scale multiply.  One step = one GEMM.  Metric TFLOP/s of 2*M*N*K.
+For N > 1 (torchrun, one process per GPU) every rank runs its own replica (the quantiser and the dense GEMM do not
+shard): value = sum over ranks of the work / the max over ranks of the device time.
+
+Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events on the launching stream; the L2 is
+flushed (256 MiB write) between steps outside the events; barrier + synchronize around the timed region; the max
+over ranks is taken.  `e2e` repeats the step through the public API from pinned host memory with the host->device
+copy of the inputs and the device->host copy of the outputs inside the timed region.
+
+--impl reference times the reference's CPU implementation of the quantiser (the oracle's C port of
+scripts/nvfp4_ref.py:71-82, all host threads) on the same config; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "NVFP4 GEMM TFLOPS & quant GB/s vs roofline; MoE tokens/s at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of the dominant kernel per launch, from the ncu captures summarised
+# under profiles/ (None until a capture exists for the workload).
+NCU_TRAFFIC = {"quant": None, "gemm": None}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", choices=["quant", "gemm"], default="quant")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
+    ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# clocks
+# ----------------------------------------------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "utilization.gpu", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, device_index: int, uuid: str | None):
+        self.proc = None
+        sel = ["--id=" + uuid] if uuid else ["--id=" + str(device_index)]
+        self.cmd = ["nvidia-smi", *sel, "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits",
+                    "-lms", "100"]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for rec in csv.reader(io.StringIO(getattr(self, "out", "") or "")):
+            if len(rec) != len(self.FIELDS):
+                continue
+            try:
+                rows.append({"sm": float(rec[0]), "max": float(rec[1]), "util": float(rec[3]),
+                             "reasons": {k: rec[i].strip() for i, k in enumerate(
+                                 ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                  "sw_power_cap"], start=4)}})
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        busy = [r for r in rows if r["util"] > 0] or rows
+        reasons = sorted({k for r in busy for k, v in r["reasons"].items() if k != "active" and v == "Active"})
+        return {"sm_mhz": statistics.median(r["sm"] for r in busy), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": reasons, "samples": len(busy)}
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# workloads
+# ----------------------------------------------------------------------------------------------------------------
+
+class QuantWorkload:
+    name = "quant"
+    unit = "GB/s"
+    dtype = "f32"     # block arithmetic (f64 for the per-block scale), bf16 in, e2m1/e4m3 out
+
+    def __init__(self, pkg, torch, orc, T=8192, K=2816):
+        self.pkg, self.torch = pkg, torch
+        self.T, self.K = T, K
+        bits = orc.synth_bf16((T, K), 1.0, seed=2024, outlier_frac=0.001)
+        self.host_bits = bits
+        import numpy as np
+        self.x = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).cuda()
+        self.amax = torch.empty(1, dtype=torch.float32, device="cuda")
+        self.packed = torch.empty((T, K // 2), dtype=torch.uint8, device="cuda")
+        self.scales = torch.empty(pkg.nvfp4_scale_buffer_bytes(T, K), dtype=torch.uint8, device="cuda")
+        self.units_per_step = T * K * 2.5625 + 4          # algorithmic bytes (SURVEY cfg1)
+        self.kernel_bytes = T * K * 2.5625                 # the quantise kernel alone (input read + outputs)
+        self.launches_per_step = 2
+        self.config = {"workload": "cfg1 activation quantiser, dynamic global scale", "T": T, "K": K,
+                       "input": "bf16 N(0,1), 0.1% entries x50", "l2": "flushed between steps (256 MiB write)"}
+
+    def step(self, ev=None):
+        p = self.pkg
+        p.amax(self.x, out=self.amax)
+        if ev is not None:
+            ev.record()
+        p.quantize(self.x, amax_dev=self.amax, packed=self.packed, scales=self.scales)
+
+    def value(self, seconds_per_step):
+        return self.units_per_step / seconds_per_step / 1e9
+
+    # end to end through the public API from pinned host buffers
+    def e2e_setup(self):
+        t = self.torch
+        self.h_x = t.empty((self.T, self.K), dtype=t.bfloat16, pin_memory=True)
+        self.h_x.copy_(self.x.cpu())
+        self.h_packed = t.empty_like(self.packed, device="cpu").pin_memory()
+        self.h_scales = t.empty_like(self.scales, device="cpu").pin_memory()
+        self.h_amax = t.empty(1, dtype=t.float32, pin_memory=True)
+        self.d_x = t.empty_like(self.x)
+        return self.T * self.K * 2, self.packed.numel() + self.scales.numel() + 4
+
+    def e2e_step(self):
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        self.pkg.amax(self.d_x, out=self.amax)
+        self.pkg.quantize(self.d_x, amax_dev=self.amax, packed=self.packed, scales=self.scales)
+        self.h_packed.copy_(self.packed, non_blocking=True)
+        self.h_scales.copy_(self.scales, non_blocking=True)
+        self.h_amax.copy_(self.amax, non_blocking=True)
+
+    def cpu_run(self, native, orc, seconds):
+        """Oracle C port (all host threads) on the same input: amax + quantise, repeated for ~`seconds`."""
+        n, t0 = 0, time.perf_counter()
+        while True:
+            a = native.amax_bf16(self.host_bits)
+            native.quantize_bf16(self.host_bits, orc.global_scale_from_amax(a))
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return self.units_per_step * n / el / 1e9, f"{n} passes over cfg1 T={self.T} x K={self.K} ({el:.1f} s)"
+
+
+class GemmWorkload:
+    name = "gemm"
+    unit = "TFLOP/s"
+    dtype = "nvfp4"   # e2m1 x e2m1 with e4m3 block scales, fp32 accumulate, bf16 out
+
+    def __init__(self, pkg, torch, orc, M=8192, N=14336, K=4096):
+        import numpy as np
+        self.pkg, self.torch = pkg, torch
+        self.M, self.N, self.K = M, N, K
+        xb = orc.synth_bf16((M, K), 1.0, seed=11)
+        wb = orc.synth_bf16((N, K), 0.02, seed=12)
+        self.host_xb = xb
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+        w = torch.from_numpy(wb.view(np.int16)).view(torch.bfloat16).cuda()
+        self.amax = pkg.amax(x)
+        self.a, self.a_sf = pkg.quantize(x, amax_dev=self.amax)
+        self.gw = float(orc.global_scale_from_amax(np.abs(orc.bf16_bits_to_f32(wb)).max()))
+        self.b, self.b_sf = pkg.quantize(w, gscale=self.gw)
+        self.x = x
+        del w
+        self.out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        self.units_per_step = 2.0 * M * N * K
+        self.kernel_bytes = None
+        self.launches_per_step = 1
+        self.config = {"workload": "cfg2 dense prefill GEMM, largest config", "M": M, "N": N, "K": K,
+                       "out": "bf16 row-major, alpha fused", "l2": "flushed between steps (256 MiB write)"}
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev.record()
+        self.pkg.gemm(self.a, self.a_sf, 0.0, self.b, self.b_sf, 1.0 / self.gw, out=self.out, a_amax=self.amax)
+
+    def value(self, seconds_per_step):
+        return self.units_per_step / seconds_per_step / 1e12
+
+    def e2e_setup(self):
+        t = self.torch
+        self.h_x = t.empty((self.M, self.K), dtype=t.bfloat16, pin_memory=True)
+        self.h_x.copy_(self.x.cpu())
+        self.h_out = t.empty((self.M, self.N), dtype=t.bfloat16, pin_memory=True)
+        self.d_x = t.empty_like(self.x)
+        return self.M * self.K * 2, self.M * self.N * 2
+
+    def e2e_step(self):
+        p = self.pkg
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        p.amax(self.d_x, out=self.amax)
+        p.quantize(self.d_x, amax_dev=self.amax, packed=self.a, scales=self.a_sf)
+        p.gemm(self.a, self.a_sf, 0.0, self.b, self.b_sf, 1.0 / self.gw, out=self.out, a_amax=self.amax)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_run(self, native, orc, seconds):
+        """Oracle port: dequantise the NVFP4 operands and multiply in float64 (multithreaded BLAS) on a row sample."""
+        import numpy as np
+        rows = 64
+        px = self.a[:rows].cpu().numpy()
+        sx = orc.unswizzle_scales(self.a_sf.cpu().numpy(), self.M, self.K)[:rows]
+        pw = self.b.cpu().numpy()
+        sw = orc.unswizzle_scales(self.b_sf.cpu().numpy(), self.N, self.K)
+        gx = float(orc.global_scale_from_amax(self.amax.item()))
+        wd = orc.dequantize(pw, sw, self.gw)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            orc.dequantize(px, sx, gx) @ wd.T
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return 2.0 * rows * self.N * self.K * n / el / 1e12, f"{n} x ({rows} rows of cfg2 M x N={self.N} x K={self.K}) float64"
+
+
+# ----------------------------------------------------------------------------------------------------------------
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU quantiser (oracle C port, all host threads); rank 0 only."""
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import native
+    import nvfp4_oracle as orc
+    if args.workload != "quant":
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU arm is timed for the quant workload"}))
+        return
+    T, K = 8192, 2816
+    rows = 1024                               # bounded sample per step
+    bits = orc.synth_bf16((T, K), 1.0, seed=2024, outlier_frac=0.001)
+    sample = bits[:rows]
+    for _ in range(args.warmup):
+        native.quantize_bf16(sample, orc.global_scale_from_amax(native.amax_bf16(sample)))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        native.quantize_bf16(sample, orc.global_scale_from_amax(native.amax_bf16(sample)))
+    el = time.perf_counter() - t0
+    val = rows * K * 2.5625 * args.steps / el / 1e9
+    cores = native.num_threads()
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "cfg1 activation quantiser, dynamic global scale", "T": T, "K": K},
+        "cpu_baseline": {"value": val, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows} of {T} rows per step (C port of scripts/nvfp4_ref.py:71-82)"},
+        "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from __graft_entry__ import load_package
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import nvfp4_oracle as orc   # seeded input generation; checker helpers
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    pkg = load_package()
+    pkg.lib()
+    W = {"quant": QuantWorkload, "gemm": GemmWorkload}[args.workload](pkg, torch, orc)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    props = torch.cuda.get_device_properties(local)
+    uuid = getattr(props, "uuid", None)
+    uuid = ("GPU-" + str(uuid)) if uuid is not None and not str(uuid).startswith("GPU-") else uuid
+    sampler = ClockSampler(local, uuid)
+
+    with sampler:
+        for _ in range(args.warmup):
+            flush.zero_()
+            W.step()
+        barrier()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            W.step(mids[i])
+            stops[i].record(stream)
+        barrier()
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
+        kern_ms = [m.elapsed_time(e) for m, e in zip(mids, stops)]
+        # sustained window for the clock record (same steps, untimed)
+        t_end = time.perf_counter() + args.clock_seconds
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                flush.zero_()
+                W.step()
+            torch.cuda.synchronize()
+    clocks = sampler.summary()
+
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = W.value(ms_per_step / 1e3) * world
+
+    # end to end through the public API with host buffers
+    h2d, d2h = W.e2e_setup()
+    for _ in range(3):
+        W.e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(3, min(args.steps, 20))
+    e0.record(stream)
+    for _ in range(n_e2e):
+        W.e2e_step()
+    e1.record(stream)
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = W.value(float(te.item()) / n_e2e / 1e3) * world
+
+    peaks, peak_src = load_peaks()
+    kern_s = statistics.mean(kern_ms) / 1e3
+    if W.name == "quant":
+        achieved = W.kernel_bytes / kern_s / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["quant"],
+                "kernel": "quantize_kernel<bf16>", "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
+    else:
+        achieved = W.units_per_step / kern_s / 1e12
+        fp4_peak = peaks["bf16_tflops"] * 4.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
+                "frac": achieved / fp4_peak, "traffic": NCU_TRAFFIC["gemm"], "kernel": "gemm_nvf4_kernel",
+                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4"}
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        import native
+        cv, sample = W.cpu_run(native, orc, args.cpu_seconds)
+        cpu = {"value": cv, "unit": W.unit, "cores": native.num_threads() if W.name == "quant" else cpu_cores(),
+               "kind": "port", "sample": sample}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": W.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded, shapes of BASELINE.json configs)",
+            "config": {**W.config, "parallelism": f"replicas x{world}"},
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": W.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": W.launches_per_step * args.steps, "clocks": clocks}))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
             "nvfp4b_gemm": ([_P, _P, ctypes.c_float, _P, _P, _P, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                              ctypes.c_int, _P, ctypes.c_int, ctypes.c_longlong, _P], ctypes.c_int),
             "nvfp4b_read_device_error": ([ctypes.c_int], ctypes.c_int),
+            "nvfp4b_gemm_set_tile_config": ([ctypes.c_int], ctypes.c_int),
             "nvfp4b_w4a16_gemm": ([_P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P],
                                   ctypes.c_int),
         }
@@ -182,5 +183,157 @@ def gemm(a, a_scales, a_dequant: float, b, b_scales, b_dequant: float, out: torc
     return out
 
 
+def set_gemm_tile_config(config: int) -> None:
+    """0 = automatic, 1 = 128x256 tiles (4 stages, one accumulator), 2 = 128x128 tiles (6 stages, two)."""
+    _check("set_gemm_tile_config", lib().nvfp4b_gemm_set_tile_config(config))
+
+
 def read_device_error(reset: bool = True) -> int:
     return int(lib().nvfp4b_read_device_error(1 if reset else 0))
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# MoE (include/nvfp4_b200.h: nvfp4b_moe_*)
+# ----------------------------------------------------------------------------------------------------------------
+
+class _Experts(ctypes.Structure):
+    _fields_ = [("num_experts", ctypes.c_int), ("hidden", ctypes.c_int), ("inter", ctypes.c_int),
+                ("w13", _P), ("w13_scales", _P), ("w2", _P), ("w2_scales", _P),
+                ("w1_gscale", _P), ("w3_gscale", _P), ("w2_gscale", _P), ("a2_gscale", _P)]
+
+
+class _View(ctypes.Structure):
+    _fields_ = [(n, _P) for n in ["m_tiles", "tile_expert", "seg_start", "seg_count", "row_token", "row_weight",
+                                  "dest", "a_codes", "a_scales", "h_codes", "h_scales"]]
+
+
+def _moe_sigs():
+    L = lib()
+    if getattr(L, "_moe_ready", False):
+        return L
+    sig = {
+        "nvfp4b_moe_workspace_bytes": ([ctypes.c_int] * 5, ctypes.c_size_t),
+        "nvfp4b_moe_max_rows": ([ctypes.c_int] * 3, ctypes.c_int),
+        "nvfp4b_moe_route": ([_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P,
+                              _P, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_forward": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float, _P,
+                                _P, ctypes.c_int, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_calibrate": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float,
+                                  _P, _P, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_workspace_view": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.POINTER(_View)], ctypes.c_int),
+        "nvfp4b_moe_pack_expert": ([_P] * 6 + [ctypes.c_int, ctypes.c_int] + [_P] * 5, ctypes.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    L._moe_ready = True
+    return L
+
+
+class MoeExperts:
+    """Device arena of E experts in the layout nvfp4b_moe_forward reads (see nvfp4b_moe_experts)."""
+
+    def __init__(self, E: int, H: int, I: int, device="cuda"):
+        self.E, self.H, self.I = E, H, I
+        dev = torch.device(device)
+        self.w13 = torch.empty((E, 2 * I, H // 2), dtype=torch.uint8, device=dev)
+        self.w13_sf_bytes = nvfp4_scale_buffer_bytes(2 * I, H)
+        self.w13_scales = torch.zeros((E, self.w13_sf_bytes), dtype=torch.uint8, device=dev)
+        self.w2 = torch.empty((E, H, I // 2), dtype=torch.uint8, device=dev)
+        self.w2_sf_bytes = nvfp4_scale_buffer_bytes(H, I)
+        self.w2_scales = torch.zeros((E, self.w2_sf_bytes), dtype=torch.uint8, device=dev)
+        self.w1_gscale = torch.ones(E, dtype=torch.float32, device=dev)
+        self.w3_gscale = torch.ones(E, dtype=torch.float32, device=dev)
+        self.w2_gscale = torch.ones(E, dtype=torch.float32, device=dev)
+        self.a2_gscale = torch.ones(E, dtype=torch.float32, device=dev)
+
+    def pack(self, e: int, gate, gate_sf_logical, up, up_sf_logical, down, down_sf_logical, stream=None):
+        """Checkpoint layout (codes [N, K/2], logical e4m3 scales [N, K/16], all device uint8) -> arena slot e."""
+        _check("moe_pack_expert", _moe_sigs().nvfp4b_moe_pack_expert(
+            _ptr(gate), _ptr(gate_sf_logical), _ptr(up), _ptr(up_sf_logical), _ptr(down), _ptr(down_sf_logical),
+            self.H, self.I, _ptr(self.w13[e]), _ptr(self.w13_scales[e]), _ptr(self.w2[e]), _ptr(self.w2_scales[e]),
+            _stream(stream)))
+
+    def struct(self) -> _Experts:
+        return _Experts(self.E, self.H, self.I, _ptr(self.w13), _ptr(self.w13_scales), _ptr(self.w2),
+                        _ptr(self.w2_scales), _ptr(self.w1_gscale), _ptr(self.w3_gscale), _ptr(self.w2_gscale),
+                        _ptr(self.a2_gscale))
+
+
+def moe_workspace(T: int, H: int, I: int, E: int, topk: int, device="cuda") -> torch.Tensor:
+    n = _moe_sigs().nvfp4b_moe_workspace_bytes(T, H, I, E, topk)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def moe_max_rows(T: int, E: int, topk: int) -> int:
+    return int(_moe_sigs().nvfp4b_moe_max_rows(T, E, topk))
+
+
+def moe_route(x, proj, topk: int, workspace, per_expert_scale=None, norm: bool = False, ids=None, weights=None,
+              stream=None):
+    """Router: x [T, H] bf16, proj [E, H] bf16 -> (ids [T, topk] int32, weights [T, topk] fp32)."""
+    T, H = x.shape
+    E = proj.shape[0]
+    if ids is None:
+        ids = torch.empty((T, topk), dtype=torch.int32, device=x.device)
+    if weights is None:
+        weights = torch.empty((T, topk), dtype=torch.float32, device=x.device)
+    _check("moe_route", _moe_sigs().nvfp4b_moe_route(_ptr(x), T, H, _ptr(proj), E, topk, _ptr(per_expert_scale),
+                                                      1 if norm else 0, _ptr(ids), _ptr(weights), _ptr(workspace),
+                                                      _stream(stream)))
+    return ids, weights
+
+
+def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: float | None = None, in_amax=None,
+                out=None, accumulate: bool = False, stream=None):
+    """MoE layer (dispatch -> gate/up -> down + combine) -> out [T, H] fp32."""
+    T = x.shape[0]
+    topk = ids.shape[1]
+    if out is None:
+        out = torch.empty((T, experts.H), dtype=torch.float32, device=x.device)
+    st = experts.struct()
+    _check("moe_forward", _moe_sigs().nvfp4b_moe_forward(
+        _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
+        _ptr(out), 1 if accumulate else 0, _ptr(workspace), _stream(stream)))
+    return out
+
+
+def moe_calibrate(x, ids, weights, experts: MoeExperts, workspace, in_gscale: float | None = None, in_amax=None,
+                  stream=None):
+    """Per-expert max |h| of the gate/up output over the routed rows -> [E] fp32 device tensor."""
+    T = x.shape[0]
+    h_amax = torch.empty(experts.E, dtype=torch.float32, device=x.device)
+    st = experts.struct()
+    _check("moe_calibrate", _moe_sigs().nvfp4b_moe_calibrate(
+        _ptr(x), T, _ptr(ids), _ptr(weights), ids.shape[1], ctypes.byref(st), float(in_gscale or 0.0),
+        _ptr(in_amax), _ptr(h_amax), _ptr(workspace), _stream(stream)))
+    return h_amax
+
+
+def moe_view(workspace, T: int, H: int, I: int, E: int, topk: int) -> dict:
+    """Tensors aliasing the dispatch plan and NVFP4 buffers inside a MoE workspace (for tests and debugging)."""
+    v = _View()
+    _check("moe_view", _moe_sigs().nvfp4b_moe_workspace_view(_ptr(workspace), T, H, I, E, topk, ctypes.byref(v)))
+    rows = moe_max_rows(T, E, topk)
+    base = workspace.data_ptr()
+
+    def sl(ptr, nbytes, dtype):
+        off = ptr - base
+        return workspace[off:off + nbytes].view(dtype)
+
+    return {
+        "m_tiles": sl(v.m_tiles, 4, torch.int32),
+        "tile_expert": sl(v.tile_expert, (rows // 128) * 4, torch.int32),
+        "seg_start": sl(v.seg_start, E * 4, torch.int32),
+        "seg_count": sl(v.seg_count, E * 4, torch.int32),
+        "row_token": sl(v.row_token, rows * 4, torch.int32),
+        "row_weight": sl(v.row_weight, rows * 4, torch.float32),
+        "dest": sl(v.dest, T * topk * 4, torch.int32),
+        "a_codes": sl(v.a_codes, rows * H // 2, torch.uint8).view(rows, H // 2),
+        "a_scales": sl(v.a_scales, nvfp4_scale_buffer_bytes(rows, H), torch.uint8),
+        "h_codes": sl(v.h_codes, rows * I // 2, torch.uint8).view(rows, I // 2),
+        "h_scales": sl(v.h_scales, nvfp4_scale_buffer_bytes(rows, I), torch.uint8),
+        "rows": rows,
+    }

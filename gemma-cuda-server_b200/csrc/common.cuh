@@ -24,6 +24,9 @@ inline int launch_status() {
 // Streaming-multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// Device address of the library's error word on the current device (cached per device; NULL on failure).
+int* device_error_ptr();
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline size_t scale_bytes(int outer, int K) {
@@ -97,27 +100,47 @@ __host__ __device__ __forceinline__ float e4m3_to_float(uint32_t b) {
 
 struct BlockParams {
     uint32_t sf;    // stored e4m3 byte
-    float invL;     // fp32 estimate of 1/L (fast path)
-    double L;       // exact float64 local scale (slow path)
+    float invL;     // fp32 estimate of 1/L = g / stored (fast path)
+    float stored;   // e4m3 value of the stored scale (exact in fp32; 0 for byte 0x80)
+    float g;        // global scale
 };
 
-__device__ __forceinline__ BlockParams block_params(float bamax, float g) {
-    BlockParams p;
+// Two fp32 -> e4m3 conversions, RNE with saturation to 448: lo goes to the low byte.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float hi, float lo) {
+    uint16_t out;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(out) : "f"(hi), "f"(lo));
+    return out;
+}
+
+// Exact float64 block scale (the slow path, taken when the fp32 estimate is within 2^-20 of an e4m3 rounding
+// boundary).
+static __device__ __noinline__ uint32_t e4m3_scale_exact(float bamax, float g) {
     double stored;
     const double t = __dmul_rn((double)g, __ddiv_rn((double)bamax, 6.0));
-    p.sf = e4m3_encode_ties_low(t, &stored);
-    if (stored > 0.0) {
-        p.L = __ddiv_rn(stored, (double)g);
-        p.invL = __fdiv_rn(g, (float)stored);
-    } else {
-        p.L = 1.0;
-        p.invL = 1.0f;
-    }
+    return e4m3_encode_ties_low(t, &stored);
+}
+
+// Block scale.  t = g * bamax / 6 is estimated in fp32 (within 3 * 2^-24 relative of the reference's float64
+// value, or flushed to zero when far below the smallest e4m3 step); the estimate is scaled by (1 -/+ 2^-20) and
+// both are rounded by the hardware (RNE, saturating).  Equal results mean no e4m3 rounding boundary lies between
+// them, so that value is also the reference's ties-to-smaller rounding of the float64 t.
+__device__ __forceinline__ BlockParams block_params(float bamax, float g) {
+    BlockParams p;
+    const float t = __fmul_rn(__fmul_rn(g, bamax), 0.16666667163372039795f);
+    const uint32_t two = cvt_e4m3x2(__fmul_rn(t, 1.00000095367431640625f), __fmul_rn(t, 0.99999904632568359375f));
+    uint32_t b = two & 0xFFu;
+    if (__builtin_expect(b != (two >> 8), 0)) b = e4m3_scale_exact(bamax, g);
+    if (b == 0u) b = 0x80u;                       // a zero scale is stored as 0x80 (reference quirk)
+    p.sf = b;
+    p.g = g;
+    p.stored = e4m3_to_float(b & 0x7Fu);
+    p.invL = (b & 0x7Fu) ? __fmul_rn(g, __frcp_rn(p.stored)) : 1.0f;
     return p;
 }
 
-// Exact float64 e2m1 code of x / L (the slow path).
-static __device__ __noinline__ uint32_t e2m1_code_exact(float x, double L) {
+// Exact float64 e2m1 code of x / L (the slow path); L = stored / g, or 1 for a zero scale.
+static __device__ __noinline__ uint32_t e2m1_code_exact(float x, float stored, float g) {
+    const double L = stored > 0.0f ? __ddiv_rn((double)stored, (double)g) : 1.0;
     const double y = __ddiv_rn(fabs((double)x), L);
     const uint32_t c = (uint32_t)(y > 0.25) + (uint32_t)(y > 0.75) + (uint32_t)(y > 1.25) + (uint32_t)(y > 1.75) +
                        (uint32_t)(y > 2.5) + (uint32_t)(y > 3.5) + (uint32_t)(y > 5.0);
@@ -159,7 +182,7 @@ __device__ __forceinline__ uint32_t encode8(const float* v, const BlockParams& p
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if ((diff >> (4 * i)) & 0xFu) {
-                const uint32_t c = e2m1_code_exact(v[i], p.L);
+                const uint32_t c = e2m1_code_exact(v[i], p.stored, p.g);
                 wh = (wh & ~(0xFu << (4 * i))) | (c << (4 * i));
             }
         }

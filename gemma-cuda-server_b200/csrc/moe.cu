@@ -1,0 +1,729 @@
+// moe.cu -- MoE top-k grouped expert FFN on sm_100a (router, dispatch, grouped NVFP4 GEMMs, combine).
+//
+// Replaces the reference's device MoE (src/forward.cu:193-321: k_router_hn/scores/top8, k_moe_invert,
+// k_moe_gateup(_grouped), k_moe_down) and its orchestration moe() (src/forward.cu:516-553).  Those kernels are
+// W4A16 CUDA-core kernels that re-read every expert weight row per (token, slot); here the work is regrouped by
+// expert so each weight tile is read once per 128 routed rows and multiplied on the FP4 tensor cores:
+//
+//   1. router     logits = x @ proj^T: bf16 tcgen05 GEMM (kind::f16) split 4 ways along K into fp32 partials;
+//                 one warp per token sums the partials in a fixed order, softmax, top-k (ties -> lower id),
+//                 renormalise, x per_expert_scale (src/forward.cu:202-231 semantics).
+//   2. dispatch   a deterministic counting sort of the T*k assignments by expert: per-chunk histograms, a plan
+//                 kernel (segment starts padded to 128 rows, row-block -> expert map), and a stable rank kernel
+//                 (warp match + per-warp counts, so rows keep token order).  Replaces k_moe_invert's atomics and
+//                 its 16-row cap.
+//   3. quantise   each token row is NVFP4-quantised ONCE and its codes/scales are stored to its k destination
+//                 rows (the quantiser fused into the dispatch permutation).
+//   4. gate/up    grouped NVFP4 GEMM (gemm_core.cuh, grouped scheduler) over the expert-sorted rows; w13 rows
+//                 interleave gate and up in groups of 16 so each 32-column accumulator chunk holds 16 gate and the
+//                 matching 16 up columns; the epilogue forms gelu_tanh(gate) * up and requantises it to NVFP4 in
+//                 the layout the down GEMM reads (codes + tile-layout scales), with the expert's static scale.
+//   5. down       grouped NVFP4 GEMM; the epilogue multiplies each row by its router weight and adds it into
+//                 out[token] with 16-byte fp32 vector atomics (the weighted combine).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "gemm_core.cuh"
+#include "sm100.cuh"
+
+namespace nvfp4b {
+namespace {
+
+constexpr int kRouterSplits = 4;
+constexpr int kChunk = 4096;          // assignments per histogram / rank chunk
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int max_rows_for(int T, int E, int topk) {
+    const long long r = (long long)T * topk + (long long)E * 127;
+    return (int)((r + 127) / 128 * 128);
+}
+
+struct Workspace {
+    float* partial;
+    int* hist;
+    int* chunk_base;
+    int* seg_start;
+    int* seg_count;
+    int* m_tiles;
+    int* tile_expert;
+    int* dest;
+    int* row_token;
+    float* row_weight;
+    uint8_t* a_codes;
+    uint8_t* a_scales;
+    uint8_t* h_codes;
+    uint8_t* h_scales;
+    size_t bytes;
+};
+
+Workspace carve(void* base, int T, int H, int I, int E, int topk) {
+    Workspace w{};
+    const int n_assign = T * topk;
+    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
+    const int rows = max_rows_for(T, E, topk);
+    char* p = static_cast<char*>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char* q = p ? p + off : nullptr; off += align256(bytes); return q; };
+    w.partial = (float*)take((size_t)kRouterSplits * T * E * 4);
+    w.hist = (int*)take((size_t)n_chunks * E * 4);
+    w.chunk_base = (int*)take((size_t)n_chunks * E * 4);
+    w.seg_start = (int*)take((size_t)E * 4);
+    w.seg_count = (int*)take((size_t)E * 4);
+    w.m_tiles = (int*)take(4);
+    w.tile_expert = (int*)take((size_t)(rows / 128) * 4);
+    w.dest = (int*)take((size_t)n_assign * 4);
+    w.row_token = (int*)take((size_t)rows * 4);
+    w.row_weight = (float*)take((size_t)rows * 4);
+    w.a_codes = (uint8_t*)take((size_t)rows * (H / 2));
+    w.a_scales = (uint8_t*)take(scale_bytes(rows, H));
+    w.h_codes = (uint8_t*)take((size_t)rows * (I / 2));
+    w.h_scales = (uint8_t*)take(scale_bytes(rows, I));
+    w.bytes = off;
+    return w;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// 1. router
+// ---------------------------------------------------------------------------------------------------------------
+
+struct RouterEpi {
+    float* partial;          // [splits][T][E]
+    long long split_stride;  // T * E
+    int T, E;
+    template <int CH>
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
+                                            const uint32_t (&r)[CH][32]) const {
+        const int m = ti.a_row + row;
+        if (m >= T) return;
+        float* dst = partial + ti.split * split_stride + (long long)m * E;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int n0 = ti.n0 + col_base + 32 * c;
+            if (n0 >= E) continue;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                *reinterpret_cast<float4*>(dst + n0 + 4 * v) =
+                    make_float4(__uint_as_float(r[c][4 * v]), __uint_as_float(r[c][4 * v + 1]),
+                                __uint_as_float(r[c][4 * v + 2]), __uint_as_float(r[c][4 * v + 3]));
+        }
+    }
+};
+
+using RouterCfg = KCfg<128, 6, 2, 4, Kind::BF16>;
+
+template <int EPL>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits,
+                                                          long long split_stride, int T, int E, int topk,
+                                                          const uint16_t* __restrict__ xnorm, int H,
+                                                          const float* __restrict__ pes, int* __restrict__ ids,
+                                                          float* __restrict__ wout) {
+    const int lane = threadIdx.x & 31;
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (t >= T) return;
+    float l[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        float acc = 0.f;
+        for (int s = 0; s < splits; ++s) acc += __ldg(partial + s * split_stride + (long long)t * E + e);
+        l[i] = acc;
+    }
+    if (xnorm) {   // reference k_router_hn: x * rsqrt(mean(x^2) + 1e-6) * H^-0.5 (scale folded into proj)
+        const uint16_t* xr = xnorm + (long long)t * H;
+        float ss = 0.f;
+        for (int k = lane * 8; k < H; k += 256) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + k));
+            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float a = bf16lo(w4[i]), b = bf16hi(w4[i]);
+                ss = fmaf(a, a, ss);
+                ss = fmaf(b, b, ss);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        const float f = rsqrtf(ss / (float)H + 1e-6f) * rsqrtf((float)H);
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) l[i] *= f;
+    }
+    float mx = l[0];
+#pragma unroll
+    for (int i = 1; i < EPL; ++i) mx = fmaxf(mx, l[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    float p[EPL], sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) { p[i] = expf(l[i] - mx); sum += p[i]; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) p[i] = p[i] / sum;
+    unsigned used = 0u;
+    int my_id = 0;
+    float my_p = 0.f, wsum = 0.f;
+    for (int j = 0; j < topk; ++j) {
+        float bv = -1.f;
+        int be = 0x7FFFFFFF;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+            if (!((used >> i) & 1u) && p[i] > bv) { bv = p[i]; be = lane + 32 * i; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+            const int oe = __shfl_xor_sync(0xFFFFFFFFu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        if ((be & 31) == lane) used |= 1u << (be >> 5);
+        if (lane == j) { my_id = be; my_p = bv; }
+        wsum += bv;
+    }
+    if (lane < topk) {
+        float w = my_p / wsum;
+        if (pes) w *= __ldg(pes + my_id);
+        ids[(long long)t * topk + lane] = my_id;
+        wout[(long long)t * topk + lane] = w;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// 2. dispatch
+// ---------------------------------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) moe_hist_kernel(const int* __restrict__ ids, int n_assign, int E,
+                                                       int* __restrict__ hist) {
+    __shared__ int h[256];
+    for (int i = threadIdx.x; i < E; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    const int base = blockIdx.x * kChunk;
+    const int end = min(base + kChunk, n_assign);
+    for (int a = base + threadIdx.x; a < end; a += blockDim.x) {
+        const int e = __ldg(ids + a);
+        if (e >= 0 && e < E) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += blockDim.x) hist[blockIdx.x * E + i] = h[i];
+}
+
+__global__ void __launch_bounds__(256) moe_plan_kernel(const int* __restrict__ hist, int n_chunks, int E,
+                                                       int* __restrict__ chunk_base, int* __restrict__ seg_start,
+                                                       int* __restrict__ seg_count, int* __restrict__ m_tiles,
+                                                       int* __restrict__ tile_expert) {
+    __shared__ int padded[257];
+    const int e = threadIdx.x;
+    int total = 0;
+    if (e < E)
+        for (int c = 0; c < n_chunks; ++c) total += hist[c * E + e];
+    padded[e + 1] = (e < E) ? (total + 127) / 128 * 128 : 0;
+    if (e == 0) padded[0] = 0;
+    __syncthreads();
+    if (e == 0)
+        for (int i = 1; i <= E; ++i) padded[i] += padded[i - 1];   // inclusive scan -> starts
+    __syncthreads();
+    if (e < E) {
+        const int start = padded[e];
+        seg_start[e] = start;
+        seg_count[e] = total;
+        int run = start;
+        for (int c = 0; c < n_chunks; ++c) {
+            chunk_base[c * E + e] = run;
+            run += hist[c * E + e];
+        }
+        for (int r = start; r < padded[e + 1]; r += 128) tile_expert[r / 128] = e;
+    }
+    if (e == 0) *m_tiles = padded[E] / 128;
+}
+
+// Stable rank of every assignment inside its expert segment: assignments are visited in index order (rounds of
+// 256, warps in order, lanes in order) so rows keep (token, slot) order.
+__global__ void __launch_bounds__(256) moe_rank_kernel(const int* __restrict__ ids, const float* __restrict__ w,
+                                                       int n_assign, int E, int topk,
+                                                       const int* __restrict__ chunk_base, int* __restrict__ dest,
+                                                       int* __restrict__ row_token, float* __restrict__ row_weight) {
+    __shared__ int run[256];
+    __shared__ int wcnt[8][256];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < E; i += 256) run[i] = chunk_base[blockIdx.x * E + i];
+    for (int i = tid; i < 8 * 256; i += 256) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    const int base = blockIdx.x * kChunk;
+    for (int round = 0; round < kChunk / 256; ++round) {
+        const int a = base + round * 256 + tid;
+        int e = -1;
+        if (a < n_assign) {
+            e = __ldg(ids + a);
+            if (e < 0 || e >= E) e = -1;
+        }
+        const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
+        __syncthreads();
+        if (e >= 0) {
+            int row = run[e] + rank;
+            for (int q = 0; q < warp; ++q) row += wcnt[q][e];
+            dest[a] = row;
+            row_token[row] = a / topk;
+            row_weight[row] = __ldg(w + a);
+        } else if (a < n_assign) {
+            dest[a] = -1;
+        }
+        __syncthreads();
+        for (int i = tid; i < E; i += 256) {
+            int s = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) { s += wcnt[q][i]; wcnt[q][i] = 0; }
+            run[i] += s;
+        }
+        __syncthreads();
+    }
+}
+
+// Padding rows of every segment: no token, zero weight, zero scales (so their products are exactly zero).
+__global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ seg_start,
+                                                      const int* __restrict__ seg_count, int kb, int tile_cols,
+                                                      uint8_t* __restrict__ a_scales, int* __restrict__ row_token,
+                                                      float* __restrict__ row_weight) {
+    const int e = blockIdx.x;
+    const int start = seg_start[e], count = seg_count[e];
+    const int pad0 = start + count, pad1 = start + (count + 127) / 128 * 128;
+    const int n = (pad1 - pad0) * kb;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int r = pad0 + i / kb, b = i % kb;
+        a_scales[((long long)(r >> 7) * tile_cols + (b >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (b & 3)] = 0;
+        if (b == 0) { row_token[r] = -1; row_weight[r] = 0.f; }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// 3. quantise once, scatter to every destination row
+// ---------------------------------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* __restrict__ x, int T, int H,
+                                                                int topk, const int* __restrict__ dest,
+                                                                float gscale, const float* __restrict__ d_amax,
+                                                                uint8_t* __restrict__ a_codes,
+                                                                uint8_t* __restrict__ a_scales, int tile_cols) {
+    const int lane = threadIdx.x & 31;
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (t >= T) return;
+    const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
+    const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
+    const int kb = H >> 4;
+    const uint16_t* xr = x + (long long)t * H;
+    for (int b = lane; b - lane < kb; b += 32) {
+        uint32_t w0 = 0, w1 = 0, sf = 0;
+        if (b < kb) {
+            const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
+            const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
+            const uint32_t ww[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { v[2 * i] = bf16lo(ww[i]); v[2 * i + 1] = bf16hi(ww[i]); }
+            sf = quantize16(v, g, w0, w1);
+        }
+        for (int j = 0; j < topk; ++j) {
+            const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
+            if (r < 0 || b >= kb) continue;
+            *reinterpret_cast<uint2*>(a_codes + (long long)r * (H >> 1) + b * 8) = make_uint2(w0, w1);
+            a_scales[((long long)(r >> 7) * tile_cols + (b >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 +
+                     (b & 3)] = (uint8_t)sf;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// 4./5. grouped GEMM epilogues
+// ---------------------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))   (kernels/elementwise.cu:44-47 of the reference)
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+template <bool CALIBRATE>
+struct GateUpEpi {
+    uint8_t* h_codes;
+    uint8_t* h_scales;
+    int I, h_tile_cols;
+    const float* w1_gscale;
+    const float* w3_gscale;
+    const float* a2_gscale;
+    float in_gscale;
+    const float* d_in_amax;
+    float* h_amax;   // calibration output
+
+    template <int CH>
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
+                                            const uint32_t (&r)[CH][32]) const {
+        const int e = ti.expert;
+        const long long m = (long long)ti.a_row + row;
+        const float gin = d_in_amax ? gscale_from_amax(__ldg(d_in_amax)) : in_gscale;
+        const float ag = __frcp_rn(gin * __ldg(w1_gscale + e));
+        const float au = __frcp_rn(gin * __ldg(w3_gscale + e));
+        const int jb0 = (ti.n0 + col_base) >> 5;          // first 16-wide block of h handled by this thread
+        if constexpr (CALIBRATE) {
+            float amax = 0.f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                if ((jb0 + c) * 16 >= I) continue;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float h = gelu_tanh(ag * __uint_as_float(r[c][i])) * (au * __uint_as_float(r[c][16 + i]));
+                    amax = fmaxf(amax, fabsf(h));
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            if ((threadIdx.x & 31) == 0 && amax > 0.f) atomicMax(reinterpret_cast<unsigned*>(h_amax + e), __float_as_uint(amax));
+        } else {
+            const float g = __ldg(a2_gscale + e);
+            uint32_t sfw = 0;
+            uint32_t cw[CH][2];
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                float h[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    h[i] = gelu_tanh(ag * __uint_as_float(r[c][i])) * (au * __uint_as_float(r[c][16 + i]));
+                const uint32_t sf = quantize16(h, g, cw[c][0], cw[c][1]);
+                sfw |= sf << (8 * c);
+            }
+            uint8_t* dst = h_codes + m * (I >> 1) + jb0 * 8;
+            const long long soff = ((m >> 7) * h_tile_cols + (jb0 >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4;
+            if (CH == 4 && (jb0 + 4) * 16 <= I) {
+                *reinterpret_cast<uint4*>(dst) = make_uint4(cw[0][0], cw[0][1], cw[1][0], cw[1][1]);
+                *reinterpret_cast<uint4*>(dst + 16) = make_uint4(cw[2][0], cw[2][1], cw[3][0], cw[3][1]);
+                *reinterpret_cast<uint32_t*>(h_scales + soff) = sfw;
+            } else {
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    const int jb = jb0 + c;
+                    if (jb * 16 >= I) continue;
+                    *reinterpret_cast<uint2*>(dst + 8 * c) = make_uint2(cw[c][0], cw[c][1]);
+                    h_scales[((m >> 7) * h_tile_cols + (jb >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 +
+                             (jb & 3)] = (uint8_t)(sfw >> (8 * c));
+                }
+            }
+        }
+    }
+};
+
+struct DownEpi {
+    float* out;
+    int H;
+    const int* row_token;
+    const float* row_weight;
+    const float* w2_gscale;
+    const float* a2_gscale;
+
+    template <int CH>
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
+                                            const uint32_t (&r)[CH][32]) const {
+        const long long m = (long long)ti.a_row + row;
+        const int t = __ldg(row_token + m);
+        if (t < 0) return;
+        const int e = ti.expert;
+        const float s = __ldg(row_weight + m) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e));
+        float* dst = out + (long long)t * H;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int n0 = ti.n0 + col_base + 32 * c;
+            if (n0 >= H) continue;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                atomicAdd(reinterpret_cast<float4*>(dst + n0 + 4 * v),
+                          make_float4(s * __uint_as_float(r[c][4 * v]), s * __uint_as_float(r[c][4 * v + 1]),
+                                      s * __uint_as_float(r[c][4 * v + 2]), s * __uint_as_float(r[c][4 * v + 3])));
+        }
+    }
+};
+
+using GroupCfg = KCfg<256, 4, 1, 8>;
+
+// ---------------------------------------------------------------------------------------------------------------
+// host orchestration
+// ---------------------------------------------------------------------------------------------------------------
+
+int check_experts(const nvfp4b_moe_experts* ex) {
+    if (!ex || !ex->w13 || !ex->w13_scales || !ex->w2 || !ex->w2_scales || !ex->w1_gscale || !ex->w3_gscale ||
+        !ex->w2_gscale || !ex->a2_gscale)
+        return NVFP4B_ERR_NULL;
+    if (ex->num_experts <= 0 || ex->num_experts > 256 || ex->hidden <= 0 || (ex->hidden % 256) ||
+        ex->inter <= 0 || (ex->inter % 32))
+        return NVFP4B_ERR_SHAPE;
+    if (!aligned16(ex->w13) || !aligned16(ex->w13_scales) || !aligned16(ex->w2) || !aligned16(ex->w2_scales))
+        return NVFP4B_ERR_ALIGN;
+    return NVFP4B_OK;
+}
+
+int dispatch(const void* x, int T, const int* ids, const float* weights, int topk, int H, int E, float in_gscale,
+             const float* d_in_amax, const Workspace& w, cudaStream_t s) {
+    const int n_assign = T * topk;
+    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
+    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
+    moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
+                                      w.tile_expert);
+    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
+                                             w.row_weight);
+    const int tile_cols = (H / 16 + 3) / 4;
+    moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
+                                     w.row_weight);
+    moe_quant_scatter_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
+                                                         in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols);
+    return launch_status();
+}
+
+template <bool CALIBRATE>
+int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, const float* d_in_amax, float* h_amax,
+            const Workspace& w, cudaStream_t s) {
+    const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
+    const int rows = max_rows_for(T, E, topk);
+    CUtensorMap ma, mb;
+    int st = make_kmajor_map(&ma, w.a_codes, rows, H / 2, GroupCfg::BM);
+    if (st) return st;
+    st = make_kmajor_map(&mb, ex->w13, (long long)E * 2 * I, H / 2, GroupCfg::BN);
+    if (st) return st;
+    CoreParams cp;
+    cp.err = device_error_ptr();
+    if (!cp.err) return NVFP4B_ERR_CUDA;
+    cp.sfa = w.a_scales;
+    cp.sfb = ex->w13_scales;
+    cp.tile_cols = (H / 16 + 3) / 4;
+    cp.k_tiles = (cp.tile_cols + 3) / 4;
+    GroupedSched<GroupCfg::BN> sc{};
+    sc.d_m_tiles = w.m_tiles;
+    sc.tile_expert = w.tile_expert;
+    sc.n_tiles = (2 * I + GroupCfg::BN - 1) / GroupCfg::BN;
+    sc.group_m = 8;
+    sc.n_per_expert = 2 * I;
+    sc.b_row_tiles_per_expert = (2 * I + 127) / 128;
+    sc.k_tiles = cp.k_tiles;
+    GateUpEpi<CALIBRATE> e;
+    e.h_codes = w.h_codes;
+    e.h_scales = w.h_scales;
+    e.I = I;
+    e.h_tile_cols = (I / 16 + 3) / 4;
+    e.w1_gscale = ex->w1_gscale;
+    e.w3_gscale = ex->w3_gscale;
+    e.a2_gscale = ex->a2_gscale;
+    e.in_gscale = in_gscale;
+    e.d_in_amax = d_in_amax;
+    e.h_amax = h_amax;
+    return launch_core<GroupCfg>(ma, mb, cp, sc, e, sm_count(), s);
+}
+
+int down(const nvfp4b_moe_experts* ex, int T, int topk, float* out, const Workspace& w, cudaStream_t s) {
+    const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
+    const int rows = max_rows_for(T, E, topk);
+    CUtensorMap ma, mb;
+    int st = make_kmajor_map(&ma, w.h_codes, rows, I / 2, GroupCfg::BM);
+    if (st) return st;
+    st = make_kmajor_map(&mb, ex->w2, (long long)E * H, I / 2, GroupCfg::BN);
+    if (st) return st;
+    CoreParams cp;
+    cp.err = device_error_ptr();
+    if (!cp.err) return NVFP4B_ERR_CUDA;
+    cp.sfa = w.h_scales;
+    cp.sfb = ex->w2_scales;
+    cp.tile_cols = (I / 16 + 3) / 4;
+    cp.k_tiles = (cp.tile_cols + 3) / 4;
+    GroupedSched<GroupCfg::BN> sc{};
+    sc.d_m_tiles = w.m_tiles;
+    sc.tile_expert = w.tile_expert;
+    sc.n_tiles = (H + GroupCfg::BN - 1) / GroupCfg::BN;
+    sc.group_m = 8;
+    sc.n_per_expert = H;
+    sc.b_row_tiles_per_expert = (H + 127) / 128;
+    sc.k_tiles = cp.k_tiles;
+    DownEpi e;
+    e.out = out;
+    e.H = H;
+    e.row_token = w.row_token;
+    e.row_weight = w.row_weight;
+    e.w2_gscale = ex->w2_gscale;
+    e.a2_gscale = ex->a2_gscale;
+    return launch_core<GroupCfg>(ma, mb, cp, sc, e, sm_count(), s);
+}
+
+// Gate/up interleave: w13 row 32g + r <- gate row 16g + r; 32g + 16 + r <- up row 16g + r.
+__global__ void pack_w13_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up, int I,
+                                int row_bytes, uint8_t* __restrict__ dst) {
+    const int row = blockIdx.x;     // destination row
+    const int g = row >> 5, r = row & 31;
+    const uint8_t* src = (r < 16 ? gate : up) + (long long)(16 * g + (r & 15)) * row_bytes;
+    for (int i = threadIdx.x; i < row_bytes; i += blockDim.x) dst[(long long)row * row_bytes + i] = src[i];
+}
+
+__global__ void pack_w13_scales_kernel(const uint8_t* __restrict__ gate_sf, const uint8_t* __restrict__ up_sf,
+                                       int I, int kb, int tile_cols, uint8_t* __restrict__ dst, long long total) {
+    for (long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+         o += (long long)gridDim.x * blockDim.x) {
+        const long long tile = o >> 9;
+        const int within = (int)(o & 511);
+        const int tr = (int)(tile / tile_cols), tcol = (int)(tile % tile_cols);
+        const int row = tr * 128 + ((within >> 2) & 3) * 32 + (within >> 4);
+        const int b = tcol * 4 + (within & 3);
+        uint8_t v = 0;
+        if (row < 2 * I && b < kb) {
+            const int g = row >> 5, r = row & 31;
+            const uint8_t* src = r < 16 ? gate_sf : up_sf;
+            v = src[(long long)(16 * g + (r & 15)) * kb + b];
+        }
+        dst[o] = v;
+    }
+}
+
+}  // namespace
+}  // namespace nvfp4b
+
+using namespace nvfp4b;
+
+extern "C" int nvfp4b_moe_max_rows(int T, int E, int topk) { return max_rows_for(T, E, topk); }
+
+extern "C" size_t nvfp4b_moe_workspace_bytes(int T, int H, int I, int E, int topk) {
+    if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || topk <= 0) return 0;
+    return carve(nullptr, T, H, I, E, topk).bytes;
+}
+
+extern "C" int nvfp4b_moe_workspace_view(void* workspace, int T, int H, int I, int E, int topk,
+                                         nvfp4b_moe_view* v) {
+    if (!workspace || !v) return NVFP4B_ERR_NULL;
+    const Workspace w = carve(workspace, T, H, I, E, topk);
+    v->m_tiles = w.m_tiles;
+    v->tile_expert = w.tile_expert;
+    v->seg_start = w.seg_start;
+    v->seg_count = w.seg_count;
+    v->row_token = w.row_token;
+    v->row_weight = w.row_weight;
+    v->dest = w.dest;
+    v->a_codes = w.a_codes;
+    v->a_scales = w.a_scales;
+    v->h_codes = w.h_codes;
+    v->h_scales = w.h_scales;
+    return NVFP4B_OK;
+}
+
+extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int topk,
+                                const float* per_expert_scale, int norm, int* ids, float* weights, void* workspace,
+                                void* stream) {
+    if (!x || !proj || !ids || !weights || !workspace) return NVFP4B_ERR_NULL;
+    if (T <= 0 || H <= 0 || (H % 64) || E <= 0 || (E % 32) || E > 256 || topk <= 0 || topk > 16 || topk > E)
+        return NVFP4B_ERR_SHAPE;
+    if (!aligned16(x) || !aligned16(proj) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    cudaStream_t s = (cudaStream_t)stream;
+    const Workspace w = carve(workspace, T, H, 32, E, topk);   // the router part of the layout ignores I
+    CUtensorMap ma, mb;
+    int st = make_kmajor_map(&ma, x, T, (long long)H * 2, RouterCfg::BM);
+    if (st) return st;
+    st = make_kmajor_map(&mb, proj, E, (long long)H * 2, RouterCfg::BN);
+    if (st) return st;
+    CoreParams cp;
+    cp.err = device_error_ptr();
+    if (!cp.err) return NVFP4B_ERR_CUDA;
+    cp.sfa = nullptr;
+    cp.sfb = nullptr;
+    cp.tile_cols = (H * 2) / 32;
+    cp.k_tiles = (cp.tile_cols + 3) / 4;
+    SplitKSched<RouterCfg::BN> sc{};
+    sc.m_tiles = (T + 127) / 128;
+    sc.n_tiles = (E + RouterCfg::BN - 1) / RouterCfg::BN;
+    sc.splits = kRouterSplits;
+    sc.kt_per_split = (cp.k_tiles + kRouterSplits - 1) / kRouterSplits;
+    sc.k_tiles = cp.k_tiles;
+    sc.N = E;
+    sc.b_row_tiles = (E + 127) / 128;
+    RouterEpi e;
+    e.partial = w.partial;
+    e.split_stride = (long long)T * E;
+    e.T = T;
+    e.E = E;
+    const int tiles = sc.m_tiles * sc.n_tiles * sc.splits;
+    st = launch_core<RouterCfg>(ma, mb, cp, sc, e, tiles < sm_count() ? tiles : sm_count(), s);
+    if (st) return st;
+    const unsigned blocks = (unsigned)((T + 7) / 8);
+    const uint16_t* xn = norm ? static_cast<const uint16_t*>(x) : nullptr;
+    const int epl = E / 32;
+#define NVFP4B_TOPK(EPL)                                                                                     \
+    router_topk_kernel<EPL><<<blocks, 256, 0, s>>>(w.partial, kRouterSplits, (long long)T * E, T, E, topk, xn, H, \
+                                                   per_expert_scale, ids, weights)
+    switch (epl) {
+        case 1: NVFP4B_TOPK(1); break;
+        case 2: NVFP4B_TOPK(2); break;
+        case 3: NVFP4B_TOPK(3); break;
+        case 4: NVFP4B_TOPK(4); break;
+        case 5: NVFP4B_TOPK(5); break;
+        case 6: NVFP4B_TOPK(6); break;
+        case 7: NVFP4B_TOPK(7); break;
+        default: NVFP4B_TOPK(8); break;
+    }
+#undef NVFP4B_TOPK
+    return launch_status();
+}
+
+static int moe_common_checks(const void* x, int T, const int* ids, const float* weights, int topk,
+                             const nvfp4b_moe_experts* ex, void* workspace) {
+    if (!x || !ids || !weights || !workspace) return NVFP4B_ERR_NULL;
+    const int st = check_experts(ex);
+    if (st) return st;
+    if (T <= 0 || topk <= 0 || topk > 16 || topk > ex->num_experts) return NVFP4B_ERR_SHAPE;
+    if (!aligned16(x) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    return NVFP4B_OK;
+}
+
+extern "C" int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
+                                  const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax, float* out,
+                                  int accumulate, void* workspace, void* stream) {
+    int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
+    if (st) return st;
+    if (!out) return NVFP4B_ERR_NULL;
+    if (!aligned16(out)) return NVFP4B_ERR_ALIGN;
+    cudaStream_t s = (cudaStream_t)stream;
+    const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
+    if (!accumulate) {
+        cudaError_t e = cudaMemsetAsync(out, 0, (size_t)T * ex->hidden * sizeof(float), s);
+        if (e != cudaSuccess) return record_cuda_error(e);
+    }
+    st = dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w, s);
+    if (st) return st;
+    st = gate_up<false>(ex, T, topk, in_gscale, d_in_amax, nullptr, w, s);
+    if (st) return st;
+    return down(ex, T, topk, out, w, s);
+}
+
+extern "C" int nvfp4b_moe_calibrate(const void* x, int T, const int* ids, const float* weights, int topk,
+                                    const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax,
+                                    float* h_amax, void* workspace, void* stream) {
+    int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
+    if (st) return st;
+    if (!h_amax) return NVFP4B_ERR_NULL;
+    cudaStream_t s = (cudaStream_t)stream;
+    const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
+    cudaError_t e = cudaMemsetAsync(h_amax, 0, (size_t)ex->num_experts * sizeof(float), s);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    st = dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w, s);
+    if (st) return st;
+    return gate_up<true>(ex, T, topk, in_gscale, d_in_amax, h_amax, w, s);
+}
+
+extern "C" int nvfp4b_moe_pack_expert(const uint8_t* gate, const uint8_t* gate_scales, const uint8_t* up,
+                                      const uint8_t* up_scales, const uint8_t* down_w, const uint8_t* down_scales,
+                                      int H, int I, uint8_t* w13_dst, uint8_t* w13_scales_dst, uint8_t* w2_dst,
+                                      uint8_t* w2_scales_dst, void* stream) {
+    if (!gate || !gate_scales || !up || !up_scales || !down_w || !down_scales || !w13_dst || !w13_scales_dst ||
+        !w2_dst || !w2_scales_dst)
+        return NVFP4B_ERR_NULL;
+    if (H <= 0 || I <= 0 || (H % 32) || (I % 32)) return NVFP4B_ERR_SHAPE;
+    cudaStream_t s = (cudaStream_t)stream;
+    pack_w13_kernel<<<2 * I, 128, 0, s>>>(gate, up, I, H / 2, w13_dst);
+    const long long total = (long long)scale_bytes(2 * I, H);
+    pack_w13_scales_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(gate_scales, up_scales, I, H / 16,
+                                                                           (H / 16 + 3) / 4, w13_scales_dst, total);
+    cudaError_t e = cudaMemcpyAsync(w2_dst, down_w, (size_t)H * (I / 2), cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    const int st = nvfp4b_swizzle_scales(down_scales, w2_scales_dst, H, I, stream);
+    if (st) return st;
+    return launch_status();
+}

@@ -21,53 +21,79 @@ template <typename T>
 struct InputTraits;
 
 template <>
-struct InputTraits<uint16_t> {   // bf16 bit patterns
-    static __device__ __forceinline__ void load16(const uint16_t* p, float* v) {
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+struct InputTraits<uint16_t> {   // bf16 bit patterns: 16 values = 2 x 16-byte loads
+    struct Raw { uint4 a, b; };
+    static __device__ __forceinline__ void load(const uint16_t* p, Raw& r) {
+        r.a = __ldg(reinterpret_cast<const uint4*>(p));
+        r.b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    }
+    static __device__ __forceinline__ void unpack(const Raw& r, float* v) {
+        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) { v[2 * i] = bf16lo(w[i]); v[2 * i + 1] = bf16hi(w[i]); }
     }
 };
 
 template <>
-struct InputTraits<float> {
-    static __device__ __forceinline__ void load16(const float* p, float* v) {
+struct InputTraits<float> {      // fp32: 4 x 16-byte loads
+    struct Raw { float4 q[4]; };
+    static __device__ __forceinline__ void load(const float* p, Raw& r) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r.q[i] = __ldg(reinterpret_cast<const float4*>(p) + i);
+    }
+    static __device__ __forceinline__ void unpack(const Raw& r, float* v) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(p) + i);
-            v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+            v[4 * i] = r.q[i].x; v[4 * i + 1] = r.q[i].y; v[4 * i + 2] = r.q[i].z; v[4 * i + 3] = r.q[i].w;
         }
     }
 };
 
+constexpr int kQuantCols = 4;   // scale-tile columns (64 values each) streamed by one warp
+
+// One warp per work item = (row group, chunk of kQuantCols scale-tile columns).  A row group is rows
+// {2*rp, 2*rp+1} + 32q (q = 0..3) of one 128-row tile; the warp streams along K, prefetching the next tile
+// column's 32 bytes per lane while it encodes the current one.  All index arithmetic is 32-bit except the
+// row offset, computed once per item.
 template <typename T>
-__global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, int M, int K, float gscale,
-                                                       const float* __restrict__ d_amax,
-                                                       uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
-                                                       int tile_cols, long long n_tasks) {
+__global__ void __launch_bounds__(256, 4) quantize_kernel(const T* __restrict__ x, int M, int K, float gscale,
+                                                          const float* __restrict__ d_amax,
+                                                          uint8_t* __restrict__ packed,
+                                                          uint8_t* __restrict__ scales, int tile_cols,
+                                                          int n_chunks, int n_items) {
+    using Tr = InputTraits<T>;
+    const int item = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (item >= n_items) return;
     const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
     const int lane = threadIdx.x & 31;
-    const int row_in_tile = ((lane >> 2) & 3) * 32 + (lane >> 4);   // + 2*rp
+    const int rg = item / n_chunks;
+    const int tc0 = (item - rg * n_chunks) * kQuantCols;
+    const int tc1 = min(tc0 + kQuantCols, tile_cols);
+    const int mt = rg >> 4, rp = rg & 15;
+    const int m = mt * 128 + ((lane >> 2) & 3) * 32 + 2 * rp + (lane >> 4);
     const int kb_count = K >> 4;
-    const long long warps = ((long long)gridDim.x * blockDim.x) >> 5;
-    for (long long task = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; task < n_tasks; task += warps) {
-        const int tc = (int)(task % tile_cols);
-        const long long rest = task / tile_cols;
-        const int rp = (int)(rest & 15);
-        const long long mt = rest >> 4;
-        const long long m = mt * 128 + row_in_tile + 2 * rp;
-        const int b = tc * 4 + (lane & 3);
-        uint32_t sf = 0;
-        if (m < M && b < kb_count) {
+    const bool row_ok = m < M;
+    const T* xrow = x + (size_t)(row_ok ? m : 0) * K + (lane & 3) * 16;
+    uint8_t* prow = packed + (size_t)(row_ok ? m : 0) * (K >> 1) + (lane & 3) * 8;
+    uint8_t* sf = scales + ((size_t)mt * tile_cols) * 512 + rp * 32 + lane;
+    typename Tr::Raw raw;
+    bool ok = row_ok && tc0 * 4 + (lane & 3) < kb_count;
+    if (ok) Tr::load(xrow + tc0 * 64, raw);
+    for (int tc = tc0; tc < tc1; ++tc) {
+        typename Tr::Raw nraw;
+        const bool nok = tc + 1 < tc1 && row_ok && (tc + 1) * 4 + (lane & 3) < kb_count;
+        if (nok) Tr::load(xrow + (tc + 1) * 64, nraw);
+        uint32_t b = 0;
+        if (ok) {
             float v[16];
-            InputTraits<T>::load16(x + m * K + (long long)b * 16, v);
+            Tr::unpack(raw, v);
             uint32_t w0, w1;
-            sf = quantize16(v, g, w0, w1);
-            *reinterpret_cast<uint2*>(packed + m * (K >> 1) + (long long)b * 8) = make_uint2(w0, w1);
+            b = quantize16(v, g, w0, w1);
+            *reinterpret_cast<uint2*>(prow + tc * 32) = make_uint2(w0, w1);
         }
-        scales[(mt * tile_cols + tc) * 512 + rp * 32 + lane] = (uint8_t)sf;
+        sf[tc * 512] = (uint8_t)b;
+        raw = nraw;
+        ok = nok;
     }
 }
 
@@ -79,7 +105,20 @@ __global__ void __launch_bounds__(256) amax_bf16_kernel(const uint16_t* __restri
     const long long nvec = n >> 3;
     const long long stride = (long long)gridDim.x * blockDim.x;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + 3 * stride < nvec; i += 4 * stride) {
+        uint4 a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = __ldg(xv + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            best = __vmaxu2(best, a[u].x & 0x7FFF7FFFu);
+            best = __vmaxu2(best, a[u].y & 0x7FFF7FFFu);
+            best = __vmaxu2(best, a[u].z & 0x7FFF7FFFu);
+            best = __vmaxu2(best, a[u].w & 0x7FFF7FFFu);
+        }
+    }
+    for (; i < nvec; i += stride) {
         const uint4 a = __ldg(xv + i);
         best = __vmaxu2(best, a.x & 0x7FFF7FFFu);
         best = __vmaxu2(best, a.y & 0x7FFF7FFFu);
@@ -114,12 +153,12 @@ static int launch_quantize(const T* x, int M, int K, float gscale, const float* 
     if (M <= 0 || K <= 0 || (K & 15)) return NVFP4B_ERR_SHAPE;
     if (!aligned16(x) || !aligned16(packed) || !aligned16(scales)) return NVFP4B_ERR_ALIGN;
     const int tile_cols = (K / 16 + 3) / 4;
-    const long long n_tasks = (long long)((M + 127) / 128) * 16 * tile_cols;
-    long long blocks = (n_tasks + 7) / 8;
-    const long long cap = (long long)sm_count() * 8;
-    if (blocks > cap) blocks = cap;
-    quantize_kernel<T><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed, scales,
-                                                                           tile_cols, n_tasks);
+    const int n_chunks = (tile_cols + kQuantCols - 1) / kQuantCols;
+    const long long n_items = (long long)((M + 127) / 128) * 16 * n_chunks;
+    if (n_items > (1ll << 30)) return NVFP4B_ERR_SHAPE;
+    const unsigned blocks = (unsigned)((n_items + 7) / 8);
+    quantize_kernel<T><<<blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed, scales, tile_cols,
+                                                                 n_chunks, (int)n_items);
     return launch_status();
 }
 
@@ -144,7 +183,7 @@ extern "C" int nvfp4b_amax_bf16(const void* x, long long n, float* d_amax, void*
     cudaError_t e = cudaMemsetAsync(d_amax, 0, sizeof(float), (cudaStream_t)stream);
     if (e != cudaSuccess) return record_cuda_error(e);
     long long blocks = ((n >> 3) + 255) / 256;
-    const long long cap = (long long)sm_count() * 4;
+    const long long cap = (long long)sm_count() * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     amax_bf16_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint16_t*>(x), n, d_amax);

@@ -7,6 +7,22 @@ namespace nvfp4b {
 
 static thread_local int t_last_cuda_error = 0;
 
+// Kernels whose bounded waits expire record a code here (through the pointer they are given).
+__device__ int g_device_error = 0;
+
+int* device_error_ptr() {
+    static int* cached[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!cached[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_device_error);
+        if (e != cudaSuccess) { record_cuda_error(e); return nullptr; }
+        cached[dev] = static_cast<int*>(p);
+    }
+    return cached[dev];
+}
+
 int record_cuda_error(cudaError_t e) {
     t_last_cuda_error = (int)e;
     return NVFP4B_ERR_CUDA;
@@ -33,4 +49,16 @@ extern "C" int nvfp4b_last_cuda_error(void) { return nvfp4b::t_last_cuda_error; 
 extern "C" size_t nvfp4b_scale_buffer_bytes(int outer, int K) {
     if (outer <= 0 || K <= 0) return 0;
     return nvfp4b::scale_bytes(outer, K);
+}
+
+extern "C" int nvfp4b_read_device_error(int reset) {
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, nvfp4b::g_device_error, sizeof(int));
+    if (e != cudaSuccess) return nvfp4b::record_cuda_error(e);
+    if (reset && v) {
+        const int z = 0;
+        e = cudaMemcpyToSymbol(nvfp4b::g_device_error, &z, sizeof(int));
+        if (e != cudaSuccess) return nvfp4b::record_cuda_error(e);
+    }
+    return v;
 }

@@ -162,6 +162,17 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
+// D(tmem) (+)= A(smem) * B(smem)^T, bf16 operands, fp32 accumulation (kind::f16, K = 16).
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive (once) on `bar` when every tcgen05 operation this thread issued before has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -195,6 +206,11 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
 // Scale-factor tile for tcgen05.cp 32x128b: 32 rows of 16 bytes, contiguous, no swizzle (8-row groups 128 B apart).
 __device__ __forceinline__ uint64_t desc_sf_32x16(uint32_t smem_addr) {
     return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 32) | ((uint64_t)1u << 46);
+}
+
+// kind::f16 instruction descriptor: A, B = bf16, K-major, D = f32 ([4,6) = 1), M x N (x16).
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 // kind::mxf4nvf4 block-scaled instruction descriptor: A, B = e2m1, K-major, scales ue4m3, M x N (x64).

@@ -87,6 +87,10 @@ int nvfp4b_gemm(const uint8_t* a, const uint8_t* a_scales, float a_dequant, cons
                 const uint8_t* b, const uint8_t* b_scales, float b_dequant,
                 int M, int N, int K, void* d, int out_kind, long long ldd, void* stream);
 
+/* Selects the dense GEMM tile configuration for subsequent calls in this process: 0 = automatic (default),
+ * 1 = 128x256 tiles, 4-stage pipeline, one TMEM accumulator; 2 = 128x128 tiles, 6 stages, two accumulators. */
+int nvfp4b_gemm_set_tile_config(int config);
+
 /* Reads the library's device-side error word (set by a kernel whose bounded wait expired, see
  * NVFP4B_ERR_TIMEOUT) and optionally clears it.  Synchronous (cudaMemcpyFromSymbol): not for use during capture.
  * Returns 0 if no kernel reported an error. */
@@ -100,6 +104,83 @@ int nvfp4b_read_device_error(int reset);
  * anything else a byte-granular one. */
 int nvfp4b_w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16,
                       int M, int N, int K, void* stream);
+
+/* ---- MoE top-k grouped expert FFN (replaces the router and expert kernels of src/forward.cu:193-321 and the
+ *      orchestration of moe(), src/forward.cu:516-553) ------------------------------------------------------------
+ *
+ * out[t] (+)= sum_j w[t,j] * W2_e (gelu_tanh(W1_e x_t) * (W3_e x_t)),  e = ids[t,j], j < topk
+ * with x quantised to NVFP4 once per token (global scale of the layer input) and the intermediate h quantised to
+ * NVFP4 in the gate/up epilogue with a static per-expert global scale (compressed-tensors "dynamic: local" block
+ * scales + static global scale).  Expert weights live in one arena: */
+typedef struct nvfp4b_moe_experts {
+    int num_experts;            /* E */
+    int hidden;                 /* H: model width, % 256 == 0 */
+    int inter;                  /* I: expert intermediate width, % 32 == 0 */
+    const uint8_t* w13;         /* [E, 2I, H/2] codes; rows of gate (W1) and up (W3) interleaved in groups of 16:
+                                   row 32g + r = gate row 16g + r, row 32g + 16 + r = up row 16g + r (r < 16) */
+    const uint8_t* w13_scales;  /* E consecutive tile-layout scale buffers of nvfp4b_scale_buffer_bytes(2I, H) */
+    const uint8_t* w2;          /* [E, H, I/2] codes of the down projection (W2) */
+    const uint8_t* w2_scales;   /* E consecutive scale buffers of nvfp4b_scale_buffer_bytes(H, I) */
+    const float* w1_gscale;     /* [E] device: global scales of gate, up and down weights */
+    const float* w3_gscale;
+    const float* w2_gscale;
+    const float* a2_gscale;     /* [E] device: static global scale of the down projection's input h */
+} nvfp4b_moe_experts;
+
+/* Device bytes of the workspace nvfp4b_moe_forward needs for T tokens (caller allocates, 256-byte aligned). */
+size_t nvfp4b_moe_workspace_bytes(int T, int H, int I, int E, int topk);
+
+/* Rows of the expert-sorted dispatch buffers (every expert segment padded to a multiple of 128 rows). */
+int nvfp4b_moe_max_rows(int T, int E, int topk);
+
+/* Router: logits = x @ proj^T on the tensor cores (bf16, fp32 accumulate, split along K), then per token softmax
+ * over the E experts, top-k (ties to the lower expert id), renormalised to sum 1 and multiplied by
+ * per_expert_scale[e] (if not NULL).  With norm != 0 the logits are scaled per token by H^-0.5 / rms(x) first
+ * (the reference's rmsnorm-without-weight * scale * H^-0.5, with `scale` folded into proj by the caller).
+ * x [T, H] bf16, proj [E, H] bf16; E % 32 == 0, E <= 256, topk <= 16.  ids [T, topk] int32, weights fp32. */
+int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int topk, const float* per_expert_scale,
+                     int norm, int* ids, float* weights, void* workspace, void* stream);
+
+/* Whole MoE layer: dispatch (counting sort of the T*topk assignments by expert, stable in token order),
+ * quantisation of x fused into the dispatch scatter, grouped gate/up GEMM with the gelu_tanh(gate)*up epilogue
+ * requantised to NVFP4, grouped down GEMM whose epilogue scales each row by its router weight and adds it into
+ * out[t] (fp32 [T, H]).  If accumulate == 0, out is zeroed first; otherwise the layer output is added to it
+ * (e.g. the residual stream).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale:
+ * in_gscale, or 2688 / max(*d_in_amax, 1e-9) on the device if d_in_amax is not NULL. */
+int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
+                       const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
+                       int accumulate, void* workspace, void* stream);
+
+/* Calibration pass: runs dispatch and the gate/up GEMM and writes, per expert, max |h| over the rows routed to it
+ * into h_amax[E] (device, fp32; zeroed first).  Static down-projection input scales are then 2688 / h_amax. */
+int nvfp4b_moe_calibrate(const void* x, int T, const int* ids, const float* weights, int topk,
+                         const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* h_amax,
+                         void* workspace, void* stream);
+
+/* Debug/test view of the workspace after nvfp4b_moe_forward or _calibrate: device pointers to the dispatch plan
+ * and the NVFP4 intermediate (see the field comments).  Pure pointer arithmetic, no CUDA call. */
+typedef struct nvfp4b_moe_view {
+    int* m_tiles;          /* [1] 128-row blocks in use */
+    int* tile_expert;      /* [max_rows/128] expert of each row block */
+    int* seg_start;        /* [E] first row of each expert segment */
+    int* seg_count;        /* [E] real rows of each expert */
+    int* row_token;        /* [max_rows] token of each row, -1 for padding */
+    float* row_weight;     /* [max_rows] router weight of each row */
+    int* dest;             /* [T*topk] row of each (token, slot) */
+    uint8_t* a_codes;      /* [max_rows, H/2] quantised x, expert-sorted */
+    uint8_t* a_scales;
+    uint8_t* h_codes;      /* [max_rows, I/2] quantised h */
+    uint8_t* h_scales;
+} nvfp4b_moe_view;
+int nvfp4b_moe_workspace_view(void* workspace, int T, int H, int I, int E, int topk, nvfp4b_moe_view* view);
+
+/* Packs one expert's checkpoint tensors into the arena layout: gate/up codes [I, H/2] each and their logical
+ * (unswizzled, [I, H/16]) e4m3 scales -> interleaved w13 rows + tile-layout scales; down codes are copied and its
+ * logical scales [H, I/16] swizzled.  dst pointers address expert e's slots inside the arena.  Load-time only. */
+int nvfp4b_moe_pack_expert(const uint8_t* gate, const uint8_t* gate_scales, const uint8_t* up,
+                           const uint8_t* up_scales, const uint8_t* down, const uint8_t* down_scales, int H, int I,
+                           uint8_t* w13_dst, uint8_t* w13_scales_dst, uint8_t* w2_dst, uint8_t* w2_scales_dst,
+                           void* stream);
 
 #ifdef __cplusplus
 }

@@ -303,3 +303,75 @@ def synth_bf16(shape, sigma=1.0, seed=0, outlier_frac=0.0, outlier_mult=50.0):
         sel = rng.choice(n, k, replace=False)
         x.reshape(-1)[sel] *= outlier_mult
     return f32_to_bf16_bits(x.astype(np.float32))
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# MoE, W4A4 (the device path's numerics): activations and the intermediate h are NVFP4-quantised
+# ----------------------------------------------------------------------------------------------------------------
+
+def moe_dispatch_ref(ids: np.ndarray, num_experts: int, pad: int = 128):
+    """Stable counting sort of the (token, slot) assignments by expert, each segment padded to `pad` rows.
+
+    Returns dict: seg_start [E], seg_count [E], dest [T*k] (row of each assignment), row_token [rows] (-1 = pad),
+    m_tiles.  Within a segment rows keep assignment order (token-major, slot-minor).
+    """
+    flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+    k = ids.shape[1]
+    counts = np.bincount(flat, minlength=num_experts)
+    padded = (counts + pad - 1) // pad * pad
+    start = np.concatenate([[0], np.cumsum(padded)[:-1]])
+    order = np.argsort(flat, kind="stable")
+    dest = np.empty(flat.size, np.int64)
+    rank = np.arange(flat.size) - np.concatenate([[0], np.cumsum(counts)[:-1]])[flat[order]]
+    dest[order] = start[flat[order]] + rank
+    rows = int(padded.sum())
+    row_token = np.full(rows, -1, np.int64)
+    row_token[dest] = np.arange(flat.size) // k
+    return {"seg_start": start, "seg_count": counts, "dest": dest, "row_token": row_token, "m_tiles": rows // pad}
+
+
+def gelu_tanh64(x):
+    """float64 form of gelu_tanh (scripts/ref_forward.py:75-77)."""
+    return 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3)))
+
+
+def moe_w4a4_ref(x, ids, weights, experts, g_in, g_h, h_override=None, tokens=None):
+    """W4A4 expert FFN: out[t] = sum_j w_tj * deq(Wd_e) @ deq(q(gelu_tanh(deq(Wg_e) x~) * (deq(Wu_e) x~), g_h[e]))
+    with x~ = deq(q(x, g_in)).  The structure is scripts/ref_forward.py:175-192 (experts) applied to NVFP4
+    activations; weights are NVFP4 (code * e4m3 / g).
+
+    experts: e -> dict(gate=(packed, sf_logical, g), up=(...), down=(...)).
+    h_override: e -> (h_codes_rows, h_sf_logical_rows) to use instead of quantising the float64 h (lets a test
+    check the down projection against the device's own intermediate).  tokens: restrict the output to these.
+    Returns float64 [T, H] (rows outside `tokens` are zero) and, per expert, the float64 h.
+    """
+    x = np.asarray(x, dtype=np.float64)
+    T, H = x.shape
+    k = ids.shape[1]
+    px, sx, xd = quantize_rows(x, g_in)
+    out = np.zeros((T, H), dtype=np.float64)
+    keep = np.ones(T, bool) if tokens is None else np.isin(np.arange(T), tokens)
+    hs = {}
+    for e in np.unique(ids):
+        e = int(e)
+        sel = np.nonzero((np.asarray(ids) == e) & keep[:, None])
+        if sel[0].size == 0:
+            continue
+        t_list, j_list = sel[0], sel[1]
+        order = np.lexsort((j_list, t_list))          # token-major, slot-minor (the dispatch order)
+        t_list, j_list = t_list[order], j_list[order]
+        ex = experts[e]
+        wg = dequantize(*ex["gate"])
+        wu = dequantize(*ex["up"])
+        wd = dequantize(*ex["down"])
+        xe = xd[t_list]
+        h = gelu_tanh64(xe @ wg.T) * (xe @ wu.T)
+        hs[e] = h
+        if h_override is not None and e in h_override:
+            hc, hsf = h_override[e]
+            hd = dequantize(hc, hsf, g_h[e])
+        else:
+            _, _, hd = quantize_rows(h, g_h[e])
+        y = hd @ wd.T
+        np.add.at(out, t_list, np.asarray(weights, np.float64)[t_list, j_list][:, None] * y)
+    return out, hs
