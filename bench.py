@@ -7,13 +7,15 @@ Workloads (synthetic seeded inputs with the configs' shap
   quant (default)  cfg1 at its largest size: bf16 [8192, 2816] ~ N(0,1) with 0.1% x50 outliers.  One step = device
                    global amax + NVFP4 quantise (codes, tile-layout e4m3 scales, fp32 amax).  Metric GB/s of
                    algorithmic bytes T*K*(2 + 1/2 + 1/16) + 4.
+  moe              cfg3: one MoE layer, 4096 tokens, 128 experts, top-8: router + dispatch + grouped gate/up +
+                   grouped down with the weighted combine.  Metric tokens/s.
   gemm             cfg2 at its largest size: M=8192, K=4096, N=14336, NVFP4 A and W resident, bf16 out with the
                    fused global-scale multiply.  One step = one GEMM.  Metric TFLOP/s of 2*M*N*K.
 For N > 1 (torchrun, one process per GPU) every rank runs its own replica (the quantiser and the dense GEMM do not
 shard): value = sum over ranks of the work / the max over ranks of the device time.
 
 Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events on the launching stream; the L2 is
-flushed (256 MiB write) between steps outside the events; barrier + synchronize around the timed region; the max
+flushed between steps outside the events (a 256 MiB write, then a 256 MiB read so no dirty lines remain); barrier + synchronize around the timed region; the max
 over ranks is taken.  `e2e` repeats the step through the public API from pinned host memory with the host->device
 copy of the inputs and the device->host copy of the outputs inside the timed region.
 
@@ -40,7 +42,7 @@ METRIC = "NVFP4 GEMM TFLOPS & quant GB/s vs roofline; MoE tokens/s at 1/2/4/8 B2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of the dominant kernel per launch, from the ncu captures summarised
 # under profiles/ (None until a capture exists for the workload).
-NCU_TRAFFIC = {"quant": None, "gemm": None}
+NCU_TRAFFIC = {"quant": None, "gemm": None, "moe": None}
 
 
 def parse_args():
@@ -48,7 +50,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", choices=["quant", "gemm"], default="quant")
+    ap.add_argument("--workload", choices=["quant", "gemm", "moe"], default="quant")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
@@ -138,14 +140,16 @@ class QuantWorkload:
         self.kernel_bytes = T * K * 2.5625                 # the quantise kernel alone (input read + outputs)
         self.launches_per_step = 2
         self.config = {"workload": "cfg1 activation quantiser, dynamic global scale", "T": T, "K": K,
-                       "input": "bf16 N(0,1), 0.1% entries x50", "l2": "flushed between steps (256 MiB write)"}
+                       "input": "bf16 N(0,1), 0.1% entries x50", "l2": "flushed between steps (256 MiB write + 256 MiB read)"}
 
-    def step(self, ev=None):
+    def step(self, mark=None):
         p = self.pkg
         p.amax(self.x, out=self.amax)
-        if ev is not None:
-            ev.record()
+        if mark is not None:
+            mark("kernel")
         p.quantize(self.x, amax_dev=self.amax, packed=self.packed, scales=self.scales)
+        if mark is not None:
+            mark("kernel_end")
 
     def value(self, seconds_per_step):
         return self.units_per_step / seconds_per_step / 1e9
@@ -207,12 +211,14 @@ class GemmWorkload:
         self.kernel_bytes = None
         self.launches_per_step = 1
         self.config = {"workload": "cfg2 dense prefill GEMM, largest config", "M": M, "N": N, "K": K,
-                       "out": "bf16 row-major, alpha fused", "l2": "flushed between steps (256 MiB write)"}
+                       "out": "bf16 row-major, alpha fused", "l2": "flushed between steps (256 MiB write + 256 MiB read)"}
 
-    def step(self, ev=None):
-        if ev is not None:
-            ev.record()
+    def step(self, mark=None):
+        if mark is not None:
+            mark("kernel")
         self.pkg.gemm(self.a, self.a_sf, 0.0, self.b, self.b_sf, 1.0 / self.gw, out=self.out, a_amax=self.amax)
+        if mark is not None:
+            mark("kernel_end")
 
     def value(self, seconds_per_step):
         return self.units_per_step / seconds_per_step / 1e12
@@ -251,6 +257,120 @@ class GemmWorkload:
             if el >= seconds:
                 break
         return 2.0 * rows * self.N * self.K * n / el / 1e12, f"{n} x ({rows} rows of cfg2 M x N={self.N} x K={self.K}) float64"
+
+
+class MoeWorkload:
+    """cfg3: one MoE FFN layer, 4096 tokens, H=2816, 128 experts (I=704), top-8, GeLU-tanh gating."""
+    name = "moe"
+    unit = "tokens/s"
+    dtype = "nvfp4"   # NVFP4 x NVFP4 grouped GEMMs, fp32 accumulate; bf16 router GEMM
+
+    def __init__(self, pkg, torch, orc, T=4096, H=2816, I=704, E=128, topk=8):
+        import numpy as np
+        self.pkg, self.torch = pkg, torch
+        self.T, self.H, self.I, self.E, self.topk = T, H, I, E, topk
+        xb = orc.synth_bf16((T, H), 1.0, seed=31)
+        rb = orc.synth_bf16((E, H), 0.02, seed=32)
+        self.x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).cuda()
+        self.proj = torch.from_numpy(rb.view(np.int16)).view(torch.bfloat16).cuda()
+        gen = torch.Generator(device="cuda").manual_seed(33)
+        arena = pkg.MoeExperts(E, H, I)
+        for e in range(E):     # N(0, 0.02) bf16 weights, NVFP4-quantised straight into the arena layout
+            w13 = (torch.randn((2 * I, H), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+            a = pkg.amax(w13)
+            g = float(orc.global_scale_from_amax(a.item()))
+            pkg.quantize(w13, gscale=g, packed=arena.w13[e], scales=arena.w13_scales[e])
+            arena.w1_gscale[e] = g
+            arena.w3_gscale[e] = g
+            w2 = (torch.randn((H, I), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+            g2 = float(orc.global_scale_from_amax(pkg.amax(w2).item()))
+            pkg.quantize(w2, gscale=g2, packed=arena.w2[e], scales=arena.w2_scales[e])
+            arena.w2_gscale[e] = g2
+        self.arena = arena
+        self.ws = pkg.moe_workspace(T, H, I, E, topk)
+        self.in_amax = pkg.amax(self.x)
+        self.ids, self.wts = pkg.moe_route(self.x, self.proj, topk, self.ws)
+        h_amax = pkg.moe_calibrate(self.x, self.ids, self.wts, arena, self.ws, in_amax=self.in_amax)
+        torch.cuda.synchronize()
+        arena.a2_gscale.copy_(torch.from_numpy(np.array([orc.global_scale_from_amax(v) for v in h_amax.cpu().numpy()],
+                                                        np.float32)))
+        self.out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        self.units_per_step = T
+        self.kernel_flops = 2.0 * T * topk * (2 * I) * H          # grouped gate/up GEMM, routed rows only
+        self.step_flops = 2.0 * T * topk * 3 * I * H + 2.0 * T * E * H
+        self.launches_per_step = 11   # amax, router GEMM + top-k, hist/plan/rank/pad/scatter, gate/up, down
+        self.config = {"workload": "cfg3 MoE FFN layer", "tokens": T, "hidden": H, "experts": E, "inter": I,
+                       "topk": topk, "router": "bf16 [128, 2816], softmax-top8-renorm",
+                       "scales": "x: dynamic global (device amax); h: static per-expert (calibrated once)",
+                       "l2": "flushed between steps (256 MiB write + 256 MiB read)", "step_flops": self.step_flops}
+
+    def step(self, mark=None):
+        p, T, k = self.pkg, self.T, self.topk
+        p.amax(self.x, out=self.in_amax)
+        p.moe_route(self.x, self.proj, k, self.ws, ids=self.ids, weights=self.wts)
+        p.moe_dispatch(self.x, self.ids, self.wts, self.arena, self.ws, in_amax=self.in_amax)
+        if mark is not None:
+            mark("kernel")
+        p.moe_gate_up(T, k, self.arena, self.ws, in_amax=self.in_amax)
+        if mark is not None:
+            mark("kernel_end")
+        p.moe_down(T, k, self.wts, self.arena, self.out, self.ws)    # zeroes out, then line-coalesced fp32 adds
+
+    def value(self, seconds_per_step):
+        return self.units_per_step / seconds_per_step
+
+    def e2e_setup(self):
+        t = self.torch
+        self.h_x = t.empty((self.T, self.H), dtype=t.bfloat16, pin_memory=True)
+        self.h_x.copy_(self.x.cpu())
+        self.h_out = t.empty((self.T, self.H), dtype=t.float32, pin_memory=True)
+        self.d_x = t.empty_like(self.x)
+        return self.T * self.H * 2, self.T * self.H * 4
+
+    def e2e_step(self):
+        p = self.pkg
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        p.amax(self.d_x, out=self.in_amax)
+        p.moe_route(self.d_x, self.proj, self.topk, self.ws, ids=self.ids, weights=self.wts)
+        p.moe_forward(self.d_x, self.ids, self.wts, self.arena, self.ws, in_amax=self.in_amax, out=self.out)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_run(self, native, orc, seconds):
+        """The reference's experts() semantics (scripts/ref_forward.py:175-192: dequantise each needed expert,
+        per-token loop) in W4A4 on a token sample, numpy float32."""
+        import numpy as np
+        S = 16
+        ids = self.ids[:S].cpu().numpy()
+        w = self.wts[:S].cpu().numpy()
+        x = self.x[:S].float().cpu().numpy()
+        gin = orc.global_scale_from_amax(self.in_amax.item())
+        w13 = {}
+        t0 = time.perf_counter()
+        _, _, xd = orc.quantize_rows(x.astype(np.float64), gin)
+        xd = xd.astype(np.float32)
+        out = np.zeros((S, self.H), np.float32)
+        a2 = self.arena.a2_gscale.cpu().numpy()
+        for t in range(S):
+            for j in range(self.topk):
+                e = int(ids[t, j])
+                if e not in w13:
+                    g = float(self.arena.w1_gscale[e].item())
+                    pk = self.arena.w13[e].cpu().numpy()
+                    sf = orc.unswizzle_scales(self.arena.w13_scales[e].cpu().numpy(), 2 * self.I, self.H)
+                    pd = self.arena.w2[e].cpu().numpy()
+                    sd = orc.unswizzle_scales(self.arena.w2_scales[e].cpu().numpy(), self.H, self.I)
+                    w13[e] = (orc.dequantize(pk, sf, g).astype(np.float32),
+                              orc.dequantize(pd, sd, float(self.arena.w2_gscale[e].item())).astype(np.float32))
+                wgu, wd = w13[e]
+                y = wgu @ xd[t]
+                h = orc.gelu_tanh(y.reshape(-1, 2, 16)[:, 0].reshape(-1)) * y.reshape(-1, 2, 16)[:, 1].reshape(-1)
+                _, _, hd = orc.quantize_rows(h[None].astype(np.float64), a2[e])
+                out[t] += w[t, j] * (wd @ hd[0].astype(np.float32))
+            if time.perf_counter() - t0 > seconds and t >= 1:
+                S = t + 1
+                break
+        el = time.perf_counter() - t0
+        return S / el, f"{S} tokens of cfg3 through the W4A4 experts() path (dequantised experts, float32)"
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -317,8 +437,17 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     pkg = load_package()
     pkg.lib()
-    W = {"quant": QuantWorkload, "gemm": GemmWorkload}[args.workload](pkg, torch, orc)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload}[args.workload](pkg, torch, orc)
+    # L2 flush between steps: write a 256 MiB buffer (evicts the step's data), then read another 256 MiB buffer so
+    # the L2 is left holding clean lines (otherwise the next step would pay the flush's own write-backs).
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+
+    class _Flush:
+        def zero_(self):
+            flush_w.zero_()
+            flush_r.sum()
+    flush = _Flush()
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -337,16 +466,21 @@ def main():
             W.step()
         barrier()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        marks = [{} for _ in range(args.steps)]
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            W.step(mids[i])
+
+            def mark(name, i=i):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                marks[i][name] = ev
+            W.step(mark)
             stops[i].record(stream)
         barrier()
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
-        kern_ms = [m.elapsed_time(e) for m, e in zip(mids, stops)]
+        kern_ms = [m["kernel"].elapsed_time(m["kernel_end"]) for m in marks]
         # sustained window for the clock record (same steps, untimed)
         t_end = time.perf_counter() + args.clock_seconds
         while time.perf_counter() < t_end:
@@ -388,6 +522,14 @@ def main():
         roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["quant"],
                 "kernel": "quantize_kernel<bf16>", "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
+    elif W.name == "moe":
+        achieved = W.kernel_flops / kern_s / 1e12
+        fp4_peak = peaks["bf16_tflops"] * 4.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
+                "frac": achieved / fp4_peak, "traffic": NCU_TRAFFIC.get("moe"),
+                "kernel": "nvf4_gemm_kernel<GroupedSched, GateUpEpi> (grouped gate/up, GELU + NVFP4 requant)",
+                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
+                "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
     else:
         achieved = W.units_per_step / kern_s / 1e12
         fp4_peak = peaks["bf16_tflops"] * 4.0

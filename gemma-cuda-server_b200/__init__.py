@@ -204,7 +204,7 @@ class _Experts(ctypes.Structure):
 
 class _View(ctypes.Structure):
     _fields_ = [(n, _P) for n in ["m_tiles", "tile_expert", "seg_start", "seg_count", "row_token", "row_weight",
-                                  "dest", "a_codes", "a_scales", "h_codes", "h_scales"]]
+                                  "row_assign", "y", "dest", "a_codes", "a_scales", "h_codes", "h_scales"]]
 
 
 def _moe_sigs():
@@ -223,6 +223,12 @@ def _moe_sigs():
         "nvfp4b_moe_workspace_view": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        ctypes.POINTER(_View)], ctypes.c_int),
         "nvfp4b_moe_pack_expert": ([_P] * 6 + [ctypes.c_int, ctypes.c_int] + [_P] * 5, ctypes.c_int),
+        "nvfp4b_moe_dispatch": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float,
+                                 _P, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_gate_up": ([ctypes.c_int, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float, _P, _P, _P],
+                               ctypes.c_int),
+        "nvfp4b_moe_down": ([ctypes.c_int, ctypes.c_int, _P, ctypes.POINTER(_Experts), _P, ctypes.c_int, _P, _P],
+                            ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -286,8 +292,11 @@ def moe_route(x, proj, topk: int, workspace, per_expert_scale=None, norm: bool =
     return ids, weights
 
 
+MOE_ACCUMULATE, MOE_DETERMINISTIC = 1, 2
+
+
 def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: float | None = None, in_amax=None,
-                out=None, accumulate: bool = False, stream=None):
+                out=None, accumulate: bool = False, deterministic: bool = False, stream=None):
     """MoE layer (dispatch -> gate/up -> down + combine) -> out [T, H] fp32."""
     T = x.shape[0]
     topk = ids.shape[1]
@@ -296,8 +305,30 @@ def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: floa
     st = experts.struct()
     _check("moe_forward", _moe_sigs().nvfp4b_moe_forward(
         _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
-        _ptr(out), 1 if accumulate else 0, _ptr(workspace), _stream(stream)))
+        _ptr(out), (MOE_ACCUMULATE if accumulate else 0) | (MOE_DETERMINISTIC if deterministic else 0),
+        _ptr(workspace), _stream(stream)))
     return out
+
+
+def moe_dispatch(x, ids, weights, experts: MoeExperts, workspace, in_gscale=None, in_amax=None, stream=None):
+    st = experts.struct()
+    _check("moe_dispatch", _moe_sigs().nvfp4b_moe_dispatch(
+        _ptr(x), x.shape[0], _ptr(ids), _ptr(weights), ids.shape[1], ctypes.byref(st), float(in_gscale or 0.0),
+        _ptr(in_amax), _ptr(workspace), _stream(stream)))
+
+
+def moe_gate_up(T: int, topk: int, experts: MoeExperts, workspace, in_gscale=None, in_amax=None, stream=None):
+    st = experts.struct()
+    _check("moe_gate_up", _moe_sigs().nvfp4b_moe_gate_up(T, topk, ctypes.byref(st), float(in_gscale or 0.0),
+                                                          _ptr(in_amax), _ptr(workspace), _stream(stream)))
+
+
+def moe_down(T: int, topk: int, weights, experts: MoeExperts, out, workspace, accumulate: bool = False,
+             deterministic: bool = False, stream=None):
+    st = experts.struct()
+    flags = (MOE_ACCUMULATE if accumulate else 0) | (MOE_DETERMINISTIC if deterministic else 0)
+    _check("moe_down", _moe_sigs().nvfp4b_moe_down(T, topk, _ptr(weights), ctypes.byref(st), _ptr(out), flags,
+                                                    _ptr(workspace), _stream(stream)))
 
 
 def moe_calibrate(x, ids, weights, experts: MoeExperts, workspace, in_gscale: float | None = None, in_amax=None,
@@ -330,6 +361,7 @@ def moe_view(workspace, T: int, H: int, I: int, E: int, topk: int) -> dict:
         "seg_count": sl(v.seg_count, E * 4, torch.int32),
         "row_token": sl(v.row_token, rows * 4, torch.int32),
         "row_weight": sl(v.row_weight, rows * 4, torch.float32),
+        "row_assign": sl(v.row_assign, rows * 4, torch.int32),
         "dest": sl(v.dest, T * topk * 4, torch.int32),
         "a_codes": sl(v.a_codes, rows * H // 2, torch.uint8).view(rows, H // 2),
         "a_scales": sl(v.a_scales, nvfp4_scale_buffer_bytes(rows, H), torch.uint8),

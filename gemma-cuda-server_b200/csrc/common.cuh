@@ -204,4 +204,43 @@ __device__ __forceinline__ uint32_t quantize16(const float* v, float g, uint32_t
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Quantise one 16-element block given as 8 words of bf16 pairs (element 0 in the low half): returns the scale byte
+// and the 8 code bytes (element 0 in the low nibble of c0).  Straight-line: both bracket estimates of all 16 codes
+// are formed first and compared once; a block with any element near a rounding boundary is recomputed exactly.
+__device__ __forceinline__ uint32_t quantize16_bf16(const uint32_t (&w)[8], float g, uint32_t& c0, uint32_t& c1) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
+    m = max(m & 0xFFFFu, m >> 16);
+    const BlockParams p = block_params(__uint_as_float(m << 16), g);
+    float lo[16], hi[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float2 f = make_float2(bf16lo(w[i]), bf16hi(w[i]));
+        const float2 q = __ffma2_rn(f, make_float2(p.invL, p.invL), make_float2(0.f, 0.f));
+        const float2 l = __fmul2_rn(q, make_float2(0.99999904632568359375f, 0.99999904632568359375f));
+        const float2 h = __fmul2_rn(q, make_float2(1.00000095367431640625f, 1.00000095367431640625f));
+        lo[2 * i] = l.x; lo[2 * i + 1] = l.y;
+        hi[2 * i] = h.x; hi[2 * i + 1] = h.y;
+    }
+    const uint32_t l0 = cvt_e2m1x8(lo[0], lo[1], lo[2], lo[3], lo[4], lo[5], lo[6], lo[7]);
+    const uint32_t l1 = cvt_e2m1x8(lo[8], lo[9], lo[10], lo[11], lo[12], lo[13], lo[14], lo[15]);
+    c0 = cvt_e2m1x8(hi[0], hi[1], hi[2], hi[3], hi[4], hi[5], hi[6], hi[7]);
+    c1 = cvt_e2m1x8(hi[8], hi[9], hi[10], hi[11], hi[12], hi[13], hi[14], hi[15]);
+    if (__builtin_expect(((l0 ^ c0) | (l1 ^ c1)) != 0u, 0)) {
+        uint32_t e0 = 0, e1 = 0;
+#pragma unroll 1
+        for (int i = 0; i < 4; ++i) {
+            e0 |= (e2m1_code_exact(bf16lo(w[i]), p.stored, p.g) | (e2m1_code_exact(bf16hi(w[i]), p.stored, p.g) << 4))
+                  << (8 * i);
+            e1 |= (e2m1_code_exact(bf16lo(w[4 + i]), p.stored, p.g) |
+                   (e2m1_code_exact(bf16hi(w[4 + i]), p.stored, p.g) << 4))
+                  << (8 * i);
+        }
+        c0 = e0;
+        c1 = e1;
+    }
+    return p.sf;
+}
+
 }  // namespace nvfp4b

@@ -70,9 +70,11 @@ struct DenseEpi {
         }
     }
 
+    __device__ __forceinline__ void finish() const {}
+
     template <int CH>
-    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
-                                            const uint32_t (&r)[CH][32]) const {
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
+                                            uint8_t*) const {
         const long long m = (long long)ti.a_row + row;
         if (m >= M) return;
         const float a = d_a_amax ? __fdiv_rn(b_dequant, gscale_from_amax(__ldg(d_a_amax))) : alpha;

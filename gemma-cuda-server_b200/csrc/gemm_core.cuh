@@ -32,8 +32,9 @@ namespace nvfp4b {
 // of 128 bytes is four MMAs and the shared-memory descriptors advance by 32 bytes per MMA.
 enum class Kind { NVF4, BF16 };
 
-template <int BN_, int STAGES_, int ACC_BUFS_, int EPI_WARPS_, Kind KIND_ = Kind::NVF4>
+template <int BN_, int STAGES_, int ACC_BUFS_, int EPI_WARPS_, Kind KIND_ = Kind::NVF4, int EPI_SMEM_ = 0>
 struct KCfg {
+    static constexpr int EPI_SMEM = EPI_SMEM_;           // extra shared memory handed to the epilogue policy
     static constexpr int BM = 128, BN = BN_, STAGES = STAGES_, ACC_BUFS = ACC_BUFS_, EPI_WARPS = EPI_WARPS_;
     static constexpr Kind KIND = KIND_;
     static constexpr bool SCALED = KIND_ == Kind::NVF4;
@@ -50,8 +51,8 @@ struct KCfg {
     static constexpr int TMEM_COLS = 512;
     static constexpr int COLS_PER_WARP = BN * 4 / EPI_WARPS;
     static constexpr int CHUNKS = COLS_PER_WARP / 32;
-    static constexpr int BAR_BYTES = (2 * STAGES + 2 * ACC_BUFS) * 8 + 16;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int BAR_BYTES = ((2 * STAGES + 2 * ACC_BUFS) * 8 + 16 + 127) / 128 * 128;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_SMEM + 1024;
     static_assert(SF_COL0 + SF_COLS_A + SF_COLS_B <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(BN % 128 == 0 && BN <= 256, "BN");
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     uint64_t* tempty = tfull + C::ACC_BUFS;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + C::ACC_BUFS);
     volatile int* sflag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint8_t* esm = sSFB + C::STAGES * C::SFB_BYTES + C::BAR_BYTES;   // 128-byte aligned epilogue scratch
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -319,9 +321,10 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             }
             tc_fence_before();
             mbar_arrive(&tempty[abuf]);          // accumulator drained: the next tile's MMAs may start
-            if (col_base < ti.n_mma) epi.template process<C::CHUNKS>(ti, row, col_base, r);
+            if (col_base < ti.n_mma) epi.template process<C::CHUNKS>(ti, row, col_base, r, esm);
             if (++abuf == C::ACC_BUFS) { abuf = 0; aphase ^= 1u; }
         }
+        epi.finish();
     }
 
     tc_fence_before();

@@ -19,7 +19,8 @@
 //                 matching 16 up columns; the epilogue forms gelu_tanh(gate) * up and requantises it to NVFP4 in
 //                 the layout the down GEMM reads (codes + tile-layout scales), with the expert's static scale.
 //   5. down       grouped NVFP4 GEMM; the epilogue multiplies each row by its router weight and adds it into
-//                 out[token] with 16-byte fp32 vector atomics (the weighted combine).
+//                 out[token] (fp32) with line-coalesced reductions (a warp-level transpose through shared memory
+//                 first), or, in deterministic mode, stores fp32 rows that a combine kernel sums in slot order.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -32,7 +33,7 @@ namespace nvfp4b {
 namespace {
 
 constexpr int kRouterSplits = 4;
-constexpr int kChunk = 4096;          // assignments per histogram / rank chunk
+constexpr int kChunk = 1024;          // assignments per histogram / rank chunk
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -52,6 +53,8 @@ struct Workspace {
     int* dest;
     int* row_token;
     float* row_weight;
+    int* row_assign;
+    float* y;             // [T*topk, H] fp32 weighted expert outputs, assignment-major (deterministic combine)
     uint8_t* a_codes;
     uint8_t* a_scales;
     uint8_t* h_codes;
@@ -77,6 +80,8 @@ Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     w.dest = (int*)take((size_t)n_assign * 4);
     w.row_token = (int*)take((size_t)rows * 4);
     w.row_weight = (float*)take((size_t)rows * 4);
+    w.row_assign = (int*)take((size_t)rows * 4);
+    w.y = (float*)take((size_t)n_assign * H * 4);
     w.a_codes = (uint8_t*)take((size_t)rows * (H / 2));
     w.a_scales = (uint8_t*)take(scale_bytes(rows, H));
     w.h_codes = (uint8_t*)take((size_t)rows * (I / 2));
@@ -93,9 +98,10 @@ struct RouterEpi {
     float* partial;          // [splits][T][E]
     long long split_stride;  // T * E
     int T, E;
+    __device__ __forceinline__ void finish() const {}
     template <int CH>
-    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
-                                            const uint32_t (&r)[CH][32]) const {
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
+                                            uint8_t*) const {
         const int m = ti.a_row + row;
         if (m >= T) return;
         float* dst = partial + ti.split * split_stride + (long long)m * E;
@@ -242,7 +248,8 @@ __global__ void __launch_bounds__(256) moe_plan_kernel(const int* __restrict__ h
 __global__ void __launch_bounds__(256) moe_rank_kernel(const int* __restrict__ ids, const float* __restrict__ w,
                                                        int n_assign, int E, int topk,
                                                        const int* __restrict__ chunk_base, int* __restrict__ dest,
-                                                       int* __restrict__ row_token, float* __restrict__ row_weight) {
+                                                       int* __restrict__ row_token, float* __restrict__ row_weight,
+                                                       int* __restrict__ row_assign) {
     __shared__ int run[256];
     __shared__ int wcnt[8][256];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -267,6 +274,7 @@ __global__ void __launch_bounds__(256) moe_rank_kernel(const int* __restrict__ i
             dest[a] = row;
             row_token[row] = a / topk;
             row_weight[row] = __ldg(w + a);
+            row_assign[row] = a;
         } else if (a < n_assign) {
             dest[a] = -1;
         }
@@ -285,16 +293,18 @@ __global__ void __launch_bounds__(256) moe_rank_kernel(const int* __restrict__ i
 __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ seg_start,
                                                       const int* __restrict__ seg_count, int kb, int tile_cols,
                                                       uint8_t* __restrict__ a_scales, int* __restrict__ row_token,
-                                                      float* __restrict__ row_weight) {
+                                                      float* __restrict__ row_weight, int* __restrict__ row_assign) {
     const int e = blockIdx.x;
     const int start = seg_start[e], count = seg_count[e];
     const int pad0 = start + count, pad1 = start + (count + 127) / 128 * 128;
-    const int n = (pad1 - pad0) * kb;
+    const int n = (pad1 - pad0) * tile_cols;          // one 4-byte word = 4 blocks of one row per store
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int r = pad0 + i / kb, b = i % kb;
-        a_scales[((long long)(r >> 7) * tile_cols + (b >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (b & 3)] = 0;
-        if (b == 0) { row_token[r] = -1; row_weight[r] = 0.f; }
+        const int r = pad0 + i / tile_cols, tc = i % tile_cols;
+        *reinterpret_cast<uint32_t*>(a_scales + ((long long)(r >> 7) * tile_cols + tc) * 512 + (r & 31) * 16 +
+                                     ((r & 127) >> 5) * 4) = 0u;
+        if (tc == 0) { row_token[r] = -1; row_weight[r] = 0.f; row_assign[r] = -1; }
     }
+    (void)kb;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -319,10 +329,7 @@ __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* 
             const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
             const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
             const uint32_t ww[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { v[2 * i] = bf16lo(ww[i]); v[2 * i + 1] = bf16hi(ww[i]); }
-            sf = quantize16(v, g, w0, w1);
+            sf = quantize16_bf16(ww, g, w0, w1);
         }
         for (int j = 0; j < topk; ++j) {
             const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
@@ -354,10 +361,13 @@ struct GateUpEpi {
     float in_gscale;
     const float* d_in_amax;
     float* h_amax;   // calibration output
+    const int* row_token;
+
+    __device__ __forceinline__ void finish() const {}
 
     template <int CH>
-    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
-                                            const uint32_t (&r)[CH][32]) const {
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
+                                            uint8_t*) const {
         const int e = ti.expert;
         const long long m = (long long)ti.a_row + row;
         const float gin = d_in_amax ? gscale_from_amax(__ldg(d_in_amax)) : in_gscale;
@@ -366,9 +376,10 @@ struct GateUpEpi {
         const int jb0 = (ti.n0 + col_base) >> 5;          // first 16-wide block of h handled by this thread
         if constexpr (CALIBRATE) {
             float amax = 0.f;
+            const bool real = __ldg(row_token + m) >= 0;    // padding rows hold no token (-1)
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
-                if ((jb0 + c) * 16 >= I) continue;
+                if ((jb0 + c) * 16 >= I || !real) continue;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const float h = gelu_tanh(ag * __uint_as_float(r[c][i])) * (au * __uint_as_float(r[c][16 + i]));
@@ -411,37 +422,87 @@ struct GateUpEpi {
     }
 };
 
+// Down epilogue.  Row m holds assignment a = token * topk + slot (or -1 for padding); its contribution is
+// weight(a) / (g_h * g_w2) * acc.
+//   DETERMINISTIC = false: each warp transposes its 32-row x 32-column chunk through shared memory (32 x 33
+//     floats per warp) and then adds one row at a time into out[token, n0:n0+32] with fp32 reductions, so every
+//     warp-wide reduction covers one 128-byte line instead of 32 scattered addresses.
+//   DETERMINISTIC = true: stores the fp32 row into y[a, :] (assignment-major); moe_combine_kernel then sums each
+//     token's topk rows in slot order, giving bit-reproducible output.
+template <bool DETERMINISTIC>
 struct DownEpi {
+    float* y;
     float* out;
-    int H;
-    const int* row_token;
-    const float* row_weight;
+    int H, topk;
+    const int* row_assign;
+    const float* weights;
     const float* w2_gscale;
     const float* a2_gscale;
 
+    __device__ __forceinline__ void finish() const {}
+
     template <int CH>
-    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base,
-                                            const uint32_t (&r)[CH][32]) const {
+    __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
+                                            uint8_t* esm) const {
         const long long m = (long long)ti.a_row + row;
-        const int t = __ldg(row_token + m);
-        if (t < 0) return;
+        const int a = __ldg(row_assign + m);
         const int e = ti.expert;
-        const float s = __ldg(row_weight + m) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e));
-        float* dst = out + (long long)t * H;
+        const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
+        if constexpr (DETERMINISTIC) {
+            if (a < 0) return;
+            float* dst = y + (long long)a * H;
 #pragma unroll
-        for (int c = 0; c < CH; ++c) {
-            const int n0 = ti.n0 + col_base + 32 * c;
-            if (n0 >= H) continue;
+            for (int c = 0; c < CH; ++c) {
+                const int n0 = ti.n0 + col_base + 32 * c;
+                if (n0 >= H) continue;
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-                atomicAdd(reinterpret_cast<float4*>(dst + n0 + 4 * v),
-                          make_float4(s * __uint_as_float(r[c][4 * v]), s * __uint_as_float(r[c][4 * v + 1]),
-                                      s * __uint_as_float(r[c][4 * v + 2]), s * __uint_as_float(r[c][4 * v + 3])));
+                for (int v = 0; v < 8; ++v)
+                    *reinterpret_cast<float4*>(dst + n0 + 4 * v) =
+                        make_float4(s * __uint_as_float(r[c][4 * v]), s * __uint_as_float(r[c][4 * v + 1]),
+                                    s * __uint_as_float(r[c][4 * v + 2]), s * __uint_as_float(r[c][4 * v + 3]));
+            }
+        } else {
+            const int lane = threadIdx.x & 31;
+            float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 2) * (32 * 33);
+            const int tok = a >= 0 ? a / topk : -1;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int n0 = ti.n0 + col_base + 32 * c;     // warp-uniform
+                if (n0 >= H) continue;
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = s * __uint_as_float(r[c][i]);
+                __syncwarp();
+#pragma unroll 4
+                for (int i = 0; i < 32; ++i) {
+                    const int ti_tok = __shfl_sync(0xFFFFFFFFu, tok, i);
+                    if (ti_tok >= 0) atomicAdd(out + (long long)ti_tok * H + n0 + lane, tile[i * 33 + lane]);
+                }
+            }
         }
     }
 };
 
+// out[t] (+)= sum_j y[t*k + j] over the k slots in order, fp32.  One warp per token, 4 columns per lane step.
+__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ y, int T, int H, int topk,
+                                                          float* __restrict__ out, int accumulate) {
+    const int lane = threadIdx.x & 31;
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (t >= T) return;
+    const float* src = y + (long long)t * topk * H;
+    float* dst = out + (long long)t * H;
+    for (int c = lane * 4; c < H; c += 128) {
+        float4 acc = accumulate ? *reinterpret_cast<const float4*>(dst + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < topk; ++j) {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(src + (long long)j * H + c));
+            acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+        }
+        *reinterpret_cast<float4*>(dst + c) = acc;
+    }
+}
+
 using GroupCfg = KCfg<256, 4, 1, 8>;
+using DownCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // K = I is short: 3 stages + transpose tiles
 
 // ---------------------------------------------------------------------------------------------------------------
 // host orchestration
@@ -467,10 +528,10 @@ int dispatch(const void* x, int T, const int* ids, const float* weights, int top
     moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
                                       w.tile_expert);
     moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
-                                             w.row_weight);
+                                             w.row_weight, w.row_assign);
     const int tile_cols = (H / 16 + 3) / 4;
     moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
-                                     w.row_weight);
+                                     w.row_weight, w.row_assign);
     moe_quant_scatter_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
                                                          in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols);
     return launch_status();
@@ -512,16 +573,20 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
     e.in_gscale = in_gscale;
     e.d_in_amax = d_in_amax;
     e.h_amax = h_amax;
+    e.row_token = w.row_token;
     return launch_core<GroupCfg>(ma, mb, cp, sc, e, sm_count(), s);
 }
 
-int down(const nvfp4b_moe_experts* ex, int T, int topk, float* out, const Workspace& w, cudaStream_t s) {
+int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, float* out, int flags,
+         const Workspace& w, cudaStream_t s) {
+    const bool accumulate = (flags & NVFP4B_MOE_ACCUMULATE) != 0;
+    const bool deterministic = (flags & NVFP4B_MOE_DETERMINISTIC) != 0;
     const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
     const int rows = max_rows_for(T, E, topk);
     CUtensorMap ma, mb;
-    int st = make_kmajor_map(&ma, w.h_codes, rows, I / 2, GroupCfg::BM);
+    int st = make_kmajor_map(&ma, w.h_codes, rows, I / 2, DownCfg::BM);
     if (st) return st;
-    st = make_kmajor_map(&mb, ex->w2, (long long)E * H, I / 2, GroupCfg::BN);
+    st = make_kmajor_map(&mb, ex->w2, (long long)E * H, I / 2, DownCfg::BN);
     if (st) return st;
     CoreParams cp;
     cp.err = device_error_ptr();
@@ -530,22 +595,27 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, float* out, const Worksp
     cp.sfb = ex->w2_scales;
     cp.tile_cols = (I / 16 + 3) / 4;
     cp.k_tiles = (cp.tile_cols + 3) / 4;
-    GroupedSched<GroupCfg::BN> sc{};
+    GroupedSched<DownCfg::BN> sc{};
     sc.d_m_tiles = w.m_tiles;
     sc.tile_expert = w.tile_expert;
-    sc.n_tiles = (H + GroupCfg::BN - 1) / GroupCfg::BN;
+    sc.n_tiles = (H + DownCfg::BN - 1) / DownCfg::BN;
     sc.group_m = 8;
     sc.n_per_expert = H;
     sc.b_row_tiles_per_expert = (H + 127) / 128;
     sc.k_tiles = cp.k_tiles;
-    DownEpi e;
-    e.out = out;
-    e.H = H;
-    e.row_token = w.row_token;
-    e.row_weight = w.row_weight;
-    e.w2_gscale = ex->w2_gscale;
-    e.a2_gscale = ex->a2_gscale;
-    return launch_core<GroupCfg>(ma, mb, cp, sc, e, sm_count(), s);
+    if (deterministic) {
+        DownEpi<true> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
+        st = launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
+        if (st) return st;
+        moe_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(w.y, T, H, topk, out, accumulate ? 1 : 0);
+        return launch_status();
+    }
+    if (!accumulate) {
+        cudaError_t err = cudaMemsetAsync(out, 0, (size_t)T * H * sizeof(float), s);
+        if (err != cudaSuccess) return record_cuda_error(err);
+    }
+    DownEpi<false> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
+    return launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
 }
 
 // Gate/up interleave: w13 row 32g + r <- gate row 16g + r; 32g + 16 + r <- up row 16g + r.
@@ -598,6 +668,8 @@ extern "C" int nvfp4b_moe_workspace_view(void* workspace, int T, int H, int I, i
     v->seg_count = w.seg_count;
     v->row_token = w.row_token;
     v->row_weight = w.row_weight;
+    v->row_assign = w.row_assign;
+    v->y = w.y;
     v->dest = w.dest;
     v->a_codes = w.a_codes;
     v->a_scales = w.a_scales;
@@ -675,22 +747,49 @@ static int moe_common_checks(const void* x, int T, const int* ids, const float* 
 
 extern "C" int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
                                   const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax, float* out,
-                                  int accumulate, void* workspace, void* stream) {
+                                  int flags, void* workspace, void* stream) {
     int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
     if (st) return st;
     if (!out) return NVFP4B_ERR_NULL;
     if (!aligned16(out)) return NVFP4B_ERR_ALIGN;
     cudaStream_t s = (cudaStream_t)stream;
     const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
-    if (!accumulate) {
-        cudaError_t e = cudaMemsetAsync(out, 0, (size_t)T * ex->hidden * sizeof(float), s);
-        if (e != cudaSuccess) return record_cuda_error(e);
-    }
     st = dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w, s);
     if (st) return st;
     st = gate_up<false>(ex, T, topk, in_gscale, d_in_amax, nullptr, w, s);
     if (st) return st;
-    return down(ex, T, topk, out, w, s);
+    return down(ex, T, topk, weights, out, flags, w, s);
+}
+
+extern "C" int nvfp4b_moe_dispatch(const void* x, int T, const int* ids, const float* weights, int topk,
+                                   const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax,
+                                   void* workspace, void* stream) {
+    const int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
+    if (st) return st;
+    const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
+    return dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w,
+                    (cudaStream_t)stream);
+}
+
+extern "C" int nvfp4b_moe_gate_up(int T, int topk, const nvfp4b_moe_experts* ex, float in_gscale,
+                                  const float* d_in_amax, void* workspace, void* stream) {
+    const int st = check_experts(ex);
+    if (st) return st;
+    if (!workspace) return NVFP4B_ERR_NULL;
+    if (T <= 0 || topk <= 0 || topk > 16) return NVFP4B_ERR_SHAPE;
+    const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
+    return gate_up<false>(ex, T, topk, in_gscale, d_in_amax, nullptr, w, (cudaStream_t)stream);
+}
+
+extern "C" int nvfp4b_moe_down(int T, int topk, const float* weights, const nvfp4b_moe_experts* ex, float* out,
+                               int flags, void* workspace, void* stream) {
+    const int st = check_experts(ex);
+    if (st) return st;
+    if (!workspace || !out || !weights) return NVFP4B_ERR_NULL;
+    if (!aligned16(out)) return NVFP4B_ERR_ALIGN;
+    if (T <= 0 || topk <= 0 || topk > 16) return NVFP4B_ERR_SHAPE;
+    const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
+    return down(ex, T, topk, weights, out, flags, w, (cudaStream_t)stream);
 }
 
 extern "C" int nvfp4b_moe_calibrate(const void* x, int T, const int* ids, const float* weights, int topk,

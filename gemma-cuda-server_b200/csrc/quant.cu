@@ -3,14 +3,13 @@
 //
 // Replaces the reference's quant_kernel / nvfp4_quantize_activations (kernels/nvfp4_quant.cu:15-57), which is one
 // thread per 16-block with sixteen 4-byte loads and scattered single-byte scale stores.  Here:
-//   * work unit = one warp-task: 32 blocks = rows {r, r+1} + 32q (q = 0..3) of one 128-row tile, times the 4
-//     blocks of one 64-column scale-tile column.  Lane l handles (row 2*rp + l/16 + 32*((l/4)%4), block l%4).
-//     With that mapping the 32 scale bytes a warp produces are 32 CONSECUTIVE bytes of the tile layout
-//     (tile*512 + rp*32 + lane), so the scale store is one coalesced 32-byte write, and the 4 lanes of each row
-//     read 128 contiguous input bytes (bf16) and write 32 contiguous code bytes.
-//   * rounding is bit-exact against the reference's float64 numpy quantiser (see common.cuh).
-//   * warp-tasks are ordered scale-tile-column fastest, so consecutive warps stream consecutive input columns.
-//   * padding rows (m >= M) and padding blocks (b >= K/16) write zero scale bytes; codes only for real data.
+//   * one warp per (row, 32 consecutive 16-element blocks): each lane loads its block with two 16-byte loads, so
+//     a warp reads 1 KB of contiguous bf16 and writes 256 contiguous code bytes; its 32 scale bytes land in 8
+//     runs of 4 consecutive bytes of the 128x4-tile layout.
+//   * rounding is bit-exact against the reference's float64 numpy quantiser (see common.cuh); the per-element
+//     encode is straight-line with one exactness check per block.
+//   * padding rows (m >= M, up to the 128-row tile) and padding blocks (b >= K/16, up to the 4-block tile column)
+//     write zero scale bytes, so the whole scale buffer is written every call.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -27,10 +26,9 @@ struct InputTraits<uint16_t> {   // bf16 bit patterns: 16 values = 2 x 16-byte l
         r.a = __ldg(reinterpret_cast<const uint4*>(p));
         r.b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
     }
-    static __device__ __forceinline__ void unpack(const Raw& r, float* v) {
+    static __device__ __forceinline__ uint32_t quantize(const Raw& r, float g, uint32_t& w0, uint32_t& w1) {
         const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) { v[2 * i] = bf16lo(w[i]); v[2 * i + 1] = bf16hi(w[i]); }
+        return quantize16_bf16(w, g, w0, w1);
     }
 };
 
@@ -41,60 +39,42 @@ struct InputTraits<float> {      // fp32: 4 x 16-byte loads
 #pragma unroll
         for (int i = 0; i < 4; ++i) r.q[i] = __ldg(reinterpret_cast<const float4*>(p) + i);
     }
-    static __device__ __forceinline__ void unpack(const Raw& r, float* v) {
+    static __device__ __forceinline__ uint32_t quantize(const Raw& r, float g, uint32_t& w0, uint32_t& w1) {
+        float v[16];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             v[4 * i] = r.q[i].x; v[4 * i + 1] = r.q[i].y; v[4 * i + 2] = r.q[i].z; v[4 * i + 3] = r.q[i].w;
         }
+        return quantize16(v, g, w0, w1);
     }
 };
 
-constexpr int kQuantCols = 4;   // scale-tile columns (64 values each) streamed by one warp
-
-// One warp per work item = (row group, chunk of kQuantCols scale-tile columns).  A row group is rows
-// {2*rp, 2*rp+1} + 32q (q = 0..3) of one 128-row tile; the warp streams along K, prefetching the next tile
-// column's 32 bytes per lane while it encodes the current one.  All index arithmetic is 32-bit except the
-// row offset, computed once per item.
+// One warp per (row, 32 consecutive 16-element blocks): the warp's loads are 1 KB contiguous (bf16).  Rows are
+// padded to the 128-row tile and blocks to the 4-block tile column; padding lanes only write a zero scale byte.
+// Scale bytes go to the tile layout (4 consecutive lanes -> 4 consecutive bytes).
 template <typename T>
-__global__ void __launch_bounds__(256, 4) quantize_kernel(const T* __restrict__ x, int M, int K, float gscale,
-                                                          const float* __restrict__ d_amax,
-                                                          uint8_t* __restrict__ packed,
-                                                          uint8_t* __restrict__ scales, int tile_cols,
-                                                          int n_chunks, int n_items) {
+__global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, int M, int K, float gscale,
+                                                       const float* __restrict__ d_amax,
+                                                       uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
+                                                       int tile_cols, int chunks_per_row, int rows_padded) {
     using Tr = InputTraits<T>;
     const int item = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (item >= n_items) return;
-    const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
     const int lane = threadIdx.x & 31;
-    const int rg = item / n_chunks;
-    const int tc0 = (item - rg * n_chunks) * kQuantCols;
-    const int tc1 = min(tc0 + kQuantCols, tile_cols);
-    const int mt = rg >> 4, rp = rg & 15;
-    const int m = mt * 128 + ((lane >> 2) & 3) * 32 + 2 * rp + (lane >> 4);
-    const int kb_count = K >> 4;
-    const bool row_ok = m < M;
-    const T* xrow = x + (size_t)(row_ok ? m : 0) * K + (lane & 3) * 16;
-    uint8_t* prow = packed + (size_t)(row_ok ? m : 0) * (K >> 1) + (lane & 3) * 8;
-    uint8_t* sf = scales + ((size_t)mt * tile_cols) * 512 + rp * 32 + lane;
-    typename Tr::Raw raw;
-    bool ok = row_ok && tc0 * 4 + (lane & 3) < kb_count;
-    if (ok) Tr::load(xrow + tc0 * 64, raw);
-    for (int tc = tc0; tc < tc1; ++tc) {
-        typename Tr::Raw nraw;
-        const bool nok = tc + 1 < tc1 && row_ok && (tc + 1) * 4 + (lane & 3) < kb_count;
-        if (nok) Tr::load(xrow + (tc + 1) * 64, nraw);
-        uint32_t b = 0;
-        if (ok) {
-            float v[16];
-            Tr::unpack(raw, v);
-            uint32_t w0, w1;
-            b = quantize16(v, g, w0, w1);
-            *reinterpret_cast<uint2*>(prow + tc * 32) = make_uint2(w0, w1);
-        }
-        sf[tc * 512] = (uint8_t)b;
-        raw = nraw;
-        ok = nok;
+    const int m = item / chunks_per_row;
+    if (m >= rows_padded) return;
+    const int b = (item - m * chunks_per_row) * 32 + lane;
+    if (b >= tile_cols * 4) return;
+    uint32_t sf = 0;
+    if (m < M && b < (K >> 4)) {
+        const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
+        typename Tr::Raw raw;
+        Tr::load(x + (size_t)m * K + b * 16, raw);
+        uint32_t w0, w1;
+        sf = Tr::quantize(raw, g, w0, w1);
+        *reinterpret_cast<uint2*>(packed + (size_t)m * (K >> 1) + b * 8) = make_uint2(w0, w1);
     }
+    scales[((size_t)(m >> 7) * tile_cols + (b >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (b & 3)] =
+        (uint8_t)sf;
 }
 
 // max |x| over n bf16 values -> atomicMax on the fp32 bit pattern of d_amax (non-negative floats order like
@@ -153,12 +133,13 @@ static int launch_quantize(const T* x, int M, int K, float gscale, const float* 
     if (M <= 0 || K <= 0 || (K & 15)) return NVFP4B_ERR_SHAPE;
     if (!aligned16(x) || !aligned16(packed) || !aligned16(scales)) return NVFP4B_ERR_ALIGN;
     const int tile_cols = (K / 16 + 3) / 4;
-    const int n_chunks = (tile_cols + kQuantCols - 1) / kQuantCols;
-    const long long n_items = (long long)((M + 127) / 128) * 16 * n_chunks;
+    const int chunks_per_row = (tile_cols * 4 + 31) / 32;
+    const int rows_padded = (M + 127) / 128 * 128;
+    const long long n_items = (long long)rows_padded * chunks_per_row;
     if (n_items > (1ll << 30)) return NVFP4B_ERR_SHAPE;
     const unsigned blocks = (unsigned)((n_items + 7) / 8);
     quantize_kernel<T><<<blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed, scales, tile_cols,
-                                                                 n_chunks, (int)n_items);
+                                                                 chunks_per_row, rows_padded);
     return launch_status();
 }
 

@@ -144,12 +144,27 @@ int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int t
 /* Whole MoE layer: dispatch (counting sort of the T*topk assignments by expert, stable in token order),
  * quantisation of x fused into the dispatch scatter, grouped gate/up GEMM with the gelu_tanh(gate)*up epilogue
  * requantised to NVFP4, grouped down GEMM whose epilogue scales each row by its router weight and adds it into
- * out[t] (fp32 [T, H]).  If accumulate == 0, out is zeroed first; otherwise the layer output is added to it
- * (e.g. the residual stream).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale:
+ * out[t] (fp32 [T, H]) with line-coalesced fp32 reductions (or, with NVFP4B_MOE_DETERMINISTIC, stores fp32 rows that
+ * a combine kernel sums in slot order).  flags: NVFP4B_MOE_* (ACCUMULATE adds onto out, e.g. the residual).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale:
  * in_gscale, or 2688 / max(*d_in_amax, 1e-9) on the device if d_in_amax is not NULL. */
+enum nvfp4b_moe_flags {
+    NVFP4B_MOE_ACCUMULATE = 1,     /* add the layer output onto out instead of overwriting it */
+    NVFP4B_MOE_DETERMINISTIC = 2   /* slot-ordered fp32 combine (bit-reproducible) instead of fp32 reductions */
+};
 int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
                        const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
-                       int accumulate, void* workspace, void* stream);
+                       int flags, void* workspace, void* stream);
+
+/* The three stages of nvfp4b_moe_forward, callable one by one (same stream, same workspace, in this order):
+ * dispatch (plan + quantise-scatter of x), gate/up grouped GEMM (writes the NVFP4 intermediate), down grouped GEMM
+ * + weighted combine into out (flags as for nvfp4b_moe_forward). */
+int nvfp4b_moe_dispatch(const void* x, int T, const int* ids, const float* weights, int topk,
+                        const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, void* workspace,
+                        void* stream);
+int nvfp4b_moe_gate_up(int T, int topk, const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax,
+                       void* workspace, void* stream);
+int nvfp4b_moe_down(int T, int topk, const float* weights, const nvfp4b_moe_experts* experts, float* out,
+                    int flags, void* workspace, void* stream);
 
 /* Calibration pass: runs dispatch and the gate/up GEMM and writes, per expert, max |h| over the rows routed to it
  * into h_amax[E] (device, fp32; zeroed first).  Static down-projection input scales are then 2688 / h_amax. */
@@ -166,6 +181,8 @@ typedef struct nvfp4b_moe_view {
     int* seg_count;        /* [E] real rows of each expert */
     int* row_token;        /* [max_rows] token of each row, -1 for padding */
     float* row_weight;     /* [max_rows] router weight of each row */
+    int* row_assign;       /* [max_rows] assignment (token * topk + slot) of each row, -1 for padding */
+    float* y;              /* [T*topk, H] fp32 weighted expert outputs, assignment-major (deterministic mode) */
     int* dest;             /* [T*topk] row of each (token, slot) */
     uint8_t* a_codes;      /* [max_rows, H/2] quantised x, expert-sorted */
     uint8_t* a_scales;

@@ -1,7 +1,7 @@
 """MoE top-k grouped expert FFN on the GPU vs the CPU oracle (W4A4 restatement of scripts/ref_forward.py:160-192).
 
 Stage by stage:
-  router    ids equal to the oracle's except at near-ties (8th/9th probability gap < 1e-4), weights to 1e-4;
+  router    ids equal to the oracle's except at near-ties (8th/9th probability gap < 2e-6 relative), weights to 2e-4;
   dispatch  segment counts/starts, stable row order and the quantised dispatched rows bit-exact;
   gate/up   the requantised intermediate agrees with the oracle's quantisation of the float64 h except where h is
             within rounding distance of a code boundary (>= 99.5% of codes equal, every difference one step);
@@ -97,7 +97,7 @@ def test_router_matches_oracle(norm):
         logits = logits / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + 1e-6) * H ** -0.5
     w_ref, ids_ref = orc.route(logits.astype(np.float32), topk, pes)
     probs = np.sort(orc.softmax(logits.astype(np.float32)), axis=1)[:, ::-1]
-    clear = (probs[:, topk - 1] - probs[:, topk]) > 1e-4
+    clear = (probs[:, topk - 1] - probs[:, topk]) > 2e-6 * probs[:, topk - 1] / probs[:, topk - 1].mean()
     got_ids, got_w = ids.cpu().numpy(), w.cpu().numpy()
     assert clear.mean() > 0.9
     assert np.array_equal(got_ids[clear], ids_ref[clear])
@@ -177,15 +177,23 @@ def test_gate_up_requant_and_down_combine():
     assert rel <= 2e-2, rel
 
 
-def test_accumulate_adds_to_existing_output():
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_accumulate_and_combine_modes(deterministic):
     p, P = make_problem(64, 256, 64, 32, 4, seed=31)
     ids, w, _, _ = route_and_calibrate(p, P)
     base = torch.randn((64, 256), device="cuda", dtype=torch.float32)
-    y0 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]))
+    y0 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), deterministic=deterministic)
     y1 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), out=base.clone(),
-                       accumulate=True)
+                       accumulate=True, deterministic=deterministic)
+    y2 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]),
+                       deterministic=not deterministic)
     torch.cuda.synchronize()
     assert torch.allclose(y1, base + y0, rtol=1e-5, atol=1e-5)
+    assert torch.allclose(y0, y2, rtol=1e-5, atol=1e-6)          # the two combine modes agree
+    if deterministic:                                              # bit-reproducible
+        y3 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), deterministic=True)
+        torch.cuda.synchronize()
+        assert torch.equal(y0, y3)
 
 
 def test_cfg3_full_size_sampled_tokens():
