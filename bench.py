@@ -298,7 +298,7 @@ class MoeWorkload:
         self.units_per_step = T
         self.kernel_flops = 2.0 * T * topk * (2 * I) * H          # grouped gate/up GEMM, routed rows only
         self.step_flops = 2.0 * T * topk * 3 * I * H + 2.0 * T * E * H
-        self.launches_per_step = 11   # amax, router GEMM + top-k, hist/plan/rank/pad/scatter, gate/up, down
+        self.launches_per_step = 12   # amax, router GEMM + top-k, hist/plan/rank/pad/scatter, gate/up, down, combine
         self.config = {"workload": "cfg3 MoE FFN layer", "tokens": T, "hidden": H, "experts": E, "inter": I,
                        "topk": topk, "router": "bf16 [128, 2816], softmax-top8-renorm",
                        "scales": "x: dynamic global (device amax); h: static per-expert (calibrated once)",
@@ -314,7 +314,7 @@ class MoeWorkload:
         p.moe_gate_up(T, k, self.arena, self.ws, in_amax=self.in_amax)
         if mark is not None:
             mark("kernel_end")
-        p.moe_down(T, k, self.wts, self.arena, self.out, self.ws)    # zeroes out, then line-coalesced fp32 adds
+        p.moe_down(T, k, self.wts, self.arena, self.out, self.ws)    # fp32 row buffer + slot-ordered combine
 
     def value(self, seconds_per_step):
         return self.units_per_step / seconds_per_step

@@ -292,11 +292,11 @@ def moe_route(x, proj, topk: int, workspace, per_expert_scale=None, norm: bool =
     return ids, weights
 
 
-MOE_ACCUMULATE, MOE_DETERMINISTIC = 1, 2
+MOE_ACCUMULATE, MOE_ATOMIC = 1, 2
 
 
 def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: float | None = None, in_amax=None,
-                out=None, accumulate: bool = False, deterministic: bool = False, stream=None):
+                out=None, accumulate: bool = False, atomic: bool = False, stream=None):
     """MoE layer (dispatch -> gate/up -> down + combine) -> out [T, H] fp32."""
     T = x.shape[0]
     topk = ids.shape[1]
@@ -305,7 +305,7 @@ def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: floa
     st = experts.struct()
     _check("moe_forward", _moe_sigs().nvfp4b_moe_forward(
         _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
-        _ptr(out), (MOE_ACCUMULATE if accumulate else 0) | (MOE_DETERMINISTIC if deterministic else 0),
+        _ptr(out), (MOE_ACCUMULATE if accumulate else 0) | (MOE_ATOMIC if atomic else 0),
         _ptr(workspace), _stream(stream)))
     return out
 
@@ -324,9 +324,9 @@ def moe_gate_up(T: int, topk: int, experts: MoeExperts, workspace, in_gscale=Non
 
 
 def moe_down(T: int, topk: int, weights, experts: MoeExperts, out, workspace, accumulate: bool = False,
-             deterministic: bool = False, stream=None):
+             atomic: bool = False, stream=None):
     st = experts.struct()
-    flags = (MOE_ACCUMULATE if accumulate else 0) | (MOE_DETERMINISTIC if deterministic else 0)
+    flags = (MOE_ACCUMULATE if accumulate else 0) | (MOE_ATOMIC if atomic else 0)
     _check("moe_down", _moe_sigs().nvfp4b_moe_down(T, topk, _ptr(weights), ctypes.byref(st), _ptr(out), flags,
                                                     _ptr(workspace), _stream(stream)))
 

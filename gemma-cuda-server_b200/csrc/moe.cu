@@ -18,9 +18,10 @@
 //                 interleave gate and up in groups of 16 so each 32-column accumulator chunk holds 16 gate and the
 //                 matching 16 up columns; the epilogue forms gelu_tanh(gate) * up and requantises it to NVFP4 in
 //                 the layout the down GEMM reads (codes + tile-layout scales), with the expert's static scale.
-//   5. down       grouped NVFP4 GEMM; the epilogue multiplies each row by its router weight and adds it into
-//                 out[token] (fp32) with line-coalesced reductions (a warp-level transpose through shared memory
-//                 first), or, in deterministic mode, stores fp32 rows that a combine kernel sums in slot order.
+//   5. down       grouped NVFP4 GEMM; the epilogue multiplies each row by its router weight and stores it (fp32)
+//                 in an assignment-major buffer; a combine kernel sums each token's k rows in slot order, so the
+//                 output is bit-reproducible (an atomic-add variant exists, but the L2's fp32 atomic rate makes
+//                 it slower at these sizes).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -424,11 +425,10 @@ struct GateUpEpi {
 
 // Down epilogue.  Row m holds assignment a = token * topk + slot (or -1 for padding); its contribution is
 // weight(a) / (g_h * g_w2) * acc.
-//   DETERMINISTIC = false: each warp transposes its 32-row x 32-column chunk through shared memory (32 x 33
-//     floats per warp) and then adds one row at a time into out[token, n0:n0+32] with fp32 reductions, so every
-//     warp-wide reduction covers one 128-byte line instead of 32 scattered addresses.
-//   DETERMINISTIC = true: stores the fp32 row into y[a, :] (assignment-major); moe_combine_kernel then sums each
-//     token's topk rows in slot order, giving bit-reproducible output.
+//   DETERMINISTIC = true (default): stores the fp32 row into y[a, :] (assignment-major); moe_combine_kernel then
+//     sums each token's topk rows in slot order, giving bit-reproducible output.
+//   DETERMINISTIC = false: adds the row into out[token, :] with 16-byte fp32 vector reductions (order-dependent
+//     rounding; bounded by the L2's atomic throughput, so slower at large T*topk).
 template <bool DETERMINISTIC>
 struct DownEpi {
     float* y;
@@ -441,6 +441,8 @@ struct DownEpi {
 
     __device__ __forceinline__ void finish() const {}
 
+    // DETERMINISTIC: each warp transposes its 32-row x 32-column chunk through shared memory (32 x 33 floats) so
+    // every store instruction writes four full 128-byte row segments of y instead of 32 scattered 16-byte pieces.
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
                                             uint8_t* esm) const {
@@ -449,35 +451,39 @@ struct DownEpi {
         const int e = ti.expert;
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
+            const int lane = threadIdx.x & 31;
+            float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 2) * (32 * 33);
+            const int sub = lane >> 3, q = (lane & 7) * 4;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int n0 = ti.n0 + col_base + 32 * c;   // warp-uniform
+                if (n0 >= H) continue;
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = s * __uint_as_float(r[c][i]);
+                __syncwarp();
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                    const int i = 4 * g + sub;
+                    const int ai = __shfl_sync(0xFFFFFFFFu, a, i);
+                    const float* src = tile + i * 33 + q;
+                    if (ai >= 0)
+                        *reinterpret_cast<float4*>(y + (long long)ai * H + n0 + q) =
+                            make_float4(src[0], src[1], src[2], src[3]);
+                }
+            }
+        } else {
             if (a < 0) return;
-            float* dst = y + (long long)a * H;
+            float* dst = out + (long long)(a / topk) * H;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
                 const int n0 = ti.n0 + col_base + 32 * c;
                 if (n0 >= H) continue;
 #pragma unroll
                 for (int v = 0; v < 8; ++v)
-                    *reinterpret_cast<float4*>(dst + n0 + 4 * v) =
-                        make_float4(s * __uint_as_float(r[c][4 * v]), s * __uint_as_float(r[c][4 * v + 1]),
-                                    s * __uint_as_float(r[c][4 * v + 2]), s * __uint_as_float(r[c][4 * v + 3]));
-            }
-        } else {
-            const int lane = threadIdx.x & 31;
-            float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 2) * (32 * 33);
-            const int tok = a >= 0 ? a / topk : -1;
-#pragma unroll
-            for (int c = 0; c < CH; ++c) {
-                const int n0 = ti.n0 + col_base + 32 * c;     // warp-uniform
-                if (n0 >= H) continue;
-                __syncwarp();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = s * __uint_as_float(r[c][i]);
-                __syncwarp();
-#pragma unroll 4
-                for (int i = 0; i < 32; ++i) {
-                    const int ti_tok = __shfl_sync(0xFFFFFFFFu, tok, i);
-                    if (ti_tok >= 0) atomicAdd(out + (long long)ti_tok * H + n0 + lane, tile[i * 33 + lane]);
-                }
+                    atomicAdd(reinterpret_cast<float4*>(dst + n0 + 4 * v),
+                              make_float4(s * __uint_as_float(r[c][4 * v]), s * __uint_as_float(r[c][4 * v + 1]),
+                                          s * __uint_as_float(r[c][4 * v + 2]), s * __uint_as_float(r[c][4 * v + 3])));
             }
         }
     }
@@ -580,7 +586,7 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
 int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, float* out, int flags,
          const Workspace& w, cudaStream_t s) {
     const bool accumulate = (flags & NVFP4B_MOE_ACCUMULATE) != 0;
-    const bool deterministic = (flags & NVFP4B_MOE_DETERMINISTIC) != 0;
+    const bool deterministic = (flags & NVFP4B_MOE_ATOMIC) == 0;
     const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
     const int rows = max_rows_for(T, E, topk);
     CUtensorMap ma, mb;

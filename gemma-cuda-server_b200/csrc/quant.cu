@@ -3,9 +3,9 @@
 //
 // Replaces the reference's quant_kernel / nvfp4_quantize_activations (kernels/nvfp4_quant.cu:15-57), which is one
 // thread per 16-block with sixteen 4-byte loads and scattered single-byte scale stores.  Here:
-//   * one warp per (row, 32 consecutive 16-element blocks): each lane loads its block with two 16-byte loads, so
+//   * work item = (row, 32 consecutive 16-element blocks): each lane loads its block with two 16-byte loads, so
 //     a warp reads 1 KB of contiguous bf16 and writes 256 contiguous code bytes; its 32 scale bytes land in 8
-//     runs of 4 consecutive bytes of the 128x4-tile layout.
+//     runs of 4 consecutive bytes of the 128x4-tile layout.  Persistent warps prefetch the next item.
 //   * rounding is bit-exact against the reference's float64 numpy quantiser (see common.cuh); the per-element
 //     encode is straight-line with one exactness check per block.
 //   * padding rows (m >= M, up to the 128-row tile) and padding blocks (b >= K/16, up to the 4-block tile column)
@@ -49,38 +49,65 @@ struct InputTraits<float> {      // fp32: 4 x 16-byte loads
     }
 };
 
-// One warp per (row, 32 consecutive 16-element blocks): the warp's loads are 1 KB contiguous (bf16).  Rows are
-// padded to the 128-row tile and blocks to the 4-block tile column; padding lanes only write a zero scale byte.
-// Scale bytes go to the tile layout (4 consecutive lanes -> 4 consecutive bytes).
+// Work item = (row, 32 consecutive 16-element blocks): a warp's loads are 1 KB of contiguous bf16.  Rows are padded
+// to the 128-row tile and blocks to the 4-block tile column; padding lanes only write a zero scale byte.  Warps are
+// persistent (grid = 8 blocks per SM) and walk items with a stride, loading the next item while encoding the current
+// one, so every lane keeps 64 bytes in flight.  Scale bytes go to the tile layout (4 consecutive lanes -> 4
+// consecutive bytes).
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, int M, int K, float gscale,
                                                        const float* __restrict__ d_amax,
                                                        uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
-                                                       int tile_cols, int chunks_per_row, int rows_padded) {
+                                                       int tile_cols, int chunks_per_row, int n_items) {
     using Tr = InputTraits<T>;
-    const int item = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
-    const int m = item / chunks_per_row;
-    if (m >= rows_padded) return;
-    const int b = (item - m * chunks_per_row) * 32 + lane;
-    if (b >= tile_cols * 4) return;
-    uint32_t sf = 0;
-    if (m < M && b < (K >> 4)) {
-        const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
-        typename Tr::Raw raw;
-        Tr::load(x + (size_t)m * K + b * 16, raw);
-        uint32_t w0, w1;
-        sf = Tr::quantize(raw, g, w0, w1);
-        *reinterpret_cast<uint2*>(packed + (size_t)m * (K >> 1) + b * 8) = make_uint2(w0, w1);
+    const int warps = (int)((gridDim.x * blockDim.x) >> 5);
+    int item = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (item >= n_items) return;
+    const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
+    const int kb = K >> 4, bmax = tile_cols * 4;
+    int m = item / chunks_per_row;
+    int b = (item - m * chunks_per_row) * 32 + lane;
+    bool ok = m < M && b < kb;
+    typename Tr::Raw raw;
+    if (ok) Tr::load(x + (size_t)m * K + b * 16, raw);
+    while (true) {
+        const int nitem = item + warps;
+        const bool more = nitem < n_items;
+        int nm = 0, nb = 0;
+        bool nok = false;
+        typename Tr::Raw nraw;
+        if (more) {
+            nm = nitem / chunks_per_row;
+            nb = (nitem - nm * chunks_per_row) * 32 + lane;
+            nok = nm < M && nb < kb;
+            if (nok) Tr::load(x + (size_t)nm * K + nb * 16, nraw);
+        }
+        if (b < bmax) {
+            uint32_t sf = 0;
+            if (ok) {
+                uint32_t w0, w1;
+                sf = Tr::quantize(raw, g, w0, w1);
+                *reinterpret_cast<uint2*>(packed + (size_t)m * (K >> 1) + b * 8) = make_uint2(w0, w1);
+            }
+            scales[((size_t)(m >> 7) * tile_cols + (b >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (b & 3)] =
+                (uint8_t)sf;
+        }
+        if (!more) break;
+        item = nitem;
+        m = nm;
+        b = nb;
+        ok = nok;
+        raw = nraw;
     }
-    scales[((size_t)(m >> 7) * tile_cols + (b >> 2)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (b & 3)] =
-        (uint8_t)sf;
 }
 
-// max |x| over n bf16 values -> atomicMax on the fp32 bit pattern of d_amax (non-negative floats order like
-// their bit patterns).  d_amax must hold 0 before the launch.
+// max |x| over n bf16 values -> d_amax (fp32 bit pattern; non-negative floats order like their bit patterns).
+// Each thread keeps 4 independent 16-byte loads in flight; the block reduces in shared memory and issues ONE
+// atomicMax (same-address atomics serialise at the L2, so per-warp atomics would dominate).  d_amax must hold 0.
 __global__ void __launch_bounds__(256) amax_bf16_kernel(const uint16_t* __restrict__ x, long long n,
                                                         float* __restrict__ d_amax) {
+    __shared__ uint32_t red[8];
     uint32_t best = 0;   // max of |bf16| bit patterns, packed two per word
     const long long nvec = n >> 3;
     const long long stride = (long long)gridDim.x * blockDim.x;
@@ -105,11 +132,17 @@ __global__ void __launch_bounds__(256) amax_bf16_kernel(const uint16_t* __restri
         best = __vmaxu2(best, a.z & 0x7FFF7FFFu);
         best = __vmaxu2(best, a.w & 0x7FFF7FFFu);
     }
-    for (long long i = (nvec << 3) + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-        best = __vmaxu2(best, (uint32_t)(x[i] & 0x7FFFu));
+    for (long long k = (nvec << 3) + (long long)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += stride)
+        best = __vmaxu2(best, (uint32_t)(x[k] & 0x7FFFu));
     uint32_t m16 = max(best & 0xFFFFu, best >> 16);
     m16 = __reduce_max_sync(0xFFFFFFFFu, m16);
-    if ((threadIdx.x & 31) == 0 && m16 != 0) atomicMax(reinterpret_cast<unsigned int*>(d_amax), m16 << 16);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m16;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        uint32_t v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0u;
+        v = __reduce_max_sync(0xFFFFFFFFu, v);
+        if (threadIdx.x == 0 && v != 0) atomicMax(reinterpret_cast<unsigned int*>(d_amax), v << 16);
+    }
 }
 
 // logical [outer, K/16] -> tile layout; one thread per output byte (padding written as zero).
@@ -137,9 +170,11 @@ static int launch_quantize(const T* x, int M, int K, float gscale, const float* 
     const int rows_padded = (M + 127) / 128 * 128;
     const long long n_items = (long long)rows_padded * chunks_per_row;
     if (n_items > (1ll << 30)) return NVFP4B_ERR_SHAPE;
-    const unsigned blocks = (unsigned)((n_items + 7) / 8);
-    quantize_kernel<T><<<blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed, scales, tile_cols,
-                                                                 chunks_per_row, rows_padded);
+    long long blocks = (n_items + 7) / 8;
+    const long long cap = (long long)sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    quantize_kernel<T><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed, scales,
+                                                                           tile_cols, chunks_per_row, (int)n_items);
     return launch_status();
 }
 
@@ -163,8 +198,8 @@ extern "C" int nvfp4b_amax_bf16(const void* x, long long n, float* d_amax, void*
     if (!aligned16(x)) return NVFP4B_ERR_ALIGN;
     cudaError_t e = cudaMemsetAsync(d_amax, 0, sizeof(float), (cudaStream_t)stream);
     if (e != cudaSuccess) return record_cuda_error(e);
-    long long blocks = ((n >> 3) + 255) / 256;
-    const long long cap = (long long)sm_count() * 8;
+    long long blocks = ((n >> 3) + 1023) / 1024;
+    const long long cap = (long long)sm_count() * 2;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     amax_bf16_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint16_t*>(x), n, d_amax);

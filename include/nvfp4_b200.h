@@ -143,13 +143,14 @@ int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int t
 
 /* Whole MoE layer: dispatch (counting sort of the T*topk assignments by expert, stable in token order),
  * quantisation of x fused into the dispatch scatter, grouped gate/up GEMM with the gelu_tanh(gate)*up epilogue
- * requantised to NVFP4, grouped down GEMM whose epilogue scales each row by its router weight and adds it into
- * out[t] (fp32 [T, H]) with line-coalesced fp32 reductions (or, with NVFP4B_MOE_DETERMINISTIC, stores fp32 rows that
- * a combine kernel sums in slot order).  flags: NVFP4B_MOE_* (ACCUMULATE adds onto out, e.g. the residual).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale:
+ * requantised to NVFP4, grouped down GEMM whose epilogue scales each row by its router weight into an fp32 row
+ * buffer, and a combine summing each token's topk rows in slot order into out[t] (fp32 [T, H]; bit-reproducible).
+ * flags: NVFP4B_MOE_* (ACCUMULATE adds onto out, e.g. the residual; ATOMIC uses fp32 atomic adds instead).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale:
  * in_gscale, or 2688 / max(*d_in_amax, 1e-9) on the device if d_in_amax is not NULL. */
 enum nvfp4b_moe_flags {
-    NVFP4B_MOE_ACCUMULATE = 1,     /* add the layer output onto out instead of overwriting it */
-    NVFP4B_MOE_DETERMINISTIC = 2   /* slot-ordered fp32 combine (bit-reproducible) instead of fp32 reductions */
+    NVFP4B_MOE_ACCUMULATE = 1,  /* add the layer output onto out instead of overwriting it */
+    NVFP4B_MOE_ATOMIC = 2       /* fp32 atomic adds into out instead of the (default, bit-reproducible) slot-ordered
+                                   combine over an fp32 row buffer */
 };
 int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
                        const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
@@ -182,7 +183,7 @@ typedef struct nvfp4b_moe_view {
     int* row_token;        /* [max_rows] token of each row, -1 for padding */
     float* row_weight;     /* [max_rows] router weight of each row */
     int* row_assign;       /* [max_rows] assignment (token * topk + slot) of each row, -1 for padding */
-    float* y;              /* [T*topk, H] fp32 weighted expert outputs, assignment-major (deterministic mode) */
+    float* y;              /* [T*topk, H] fp32 weighted expert outputs, assignment-major */
     int* dest;             /* [T*topk] row of each (token, slot) */
     uint8_t* a_codes;      /* [max_rows, H/2] quantised x, expert-sorted */
     uint8_t* a_scales;

@@ -177,21 +177,20 @@ def test_gate_up_requant_and_down_combine():
     assert rel <= 2e-2, rel
 
 
-@pytest.mark.parametrize("deterministic", [False, True])
-def test_accumulate_and_combine_modes(deterministic):
+@pytest.mark.parametrize("atomic", [False, True])
+def test_accumulate_and_combine_modes(atomic):
     p, P = make_problem(64, 256, 64, 32, 4, seed=31)
     ids, w, _, _ = route_and_calibrate(p, P)
     base = torch.randn((64, 256), device="cuda", dtype=torch.float32)
-    y0 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), deterministic=deterministic)
+    y0 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), atomic=atomic)
     y1 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), out=base.clone(),
-                       accumulate=True, deterministic=deterministic)
-    y2 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]),
-                       deterministic=not deterministic)
+                       accumulate=True, atomic=atomic)
+    y2 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), atomic=not atomic)
     torch.cuda.synchronize()
     assert torch.allclose(y1, base + y0, rtol=1e-5, atol=1e-5)
     assert torch.allclose(y0, y2, rtol=1e-5, atol=1e-6)          # the two combine modes agree
-    if deterministic:                                              # bit-reproducible
-        y3 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), deterministic=True)
+    if not atomic:                                                 # the default combine is bit-reproducible
+        y3 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]))
         torch.cuda.synchronize()
         assert torch.equal(y0, y3)
 
