@@ -684,15 +684,11 @@ extern "C" int nvfp4b_moe_workspace_view(void* workspace, int T, int H, int I, i
     return NVFP4B_OK;
 }
 
-extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int topk,
-                                const float* per_expert_scale, int norm, int* ids, float* weights, void* workspace,
-                                void* stream) {
-    if (!x || !proj || !ids || !weights || !workspace) return NVFP4B_ERR_NULL;
-    if (T <= 0 || H <= 0 || (H % 64) || E <= 0 || (E % 32) || E > 256 || topk <= 0 || topk > 16 || topk > E)
-        return NVFP4B_ERR_SHAPE;
-    if (!aligned16(x) || !aligned16(proj) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
-    cudaStream_t s = (cudaStream_t)stream;
-    const Workspace w = carve(workspace, T, H, 32, E, topk);   // the router part of the layout ignores I
+// Router launch sequence (split-K bf16 GEMM into `partial`, then softmax/top-k); arguments already checked.
+// `partial` holds splits * T * E fp32 values, every one stored before it is read: nothing needs to start at zero.
+static int route_launch(const void* x, int T, int H, const void* proj, int E, int topk,
+                        const float* per_expert_scale, int norm, int* ids, float* weights, float* partial,
+                        cudaStream_t s) {
     CUtensorMap ma, mb;
     int st = make_kmajor_map(&ma, x, T, (long long)H * 2, RouterCfg::BM);
     if (st) return st;
@@ -705,16 +701,19 @@ extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, i
     cp.sfb = nullptr;
     cp.tile_cols = (H * 2) / 32;
     cp.k_tiles = (cp.tile_cols + 3) / 4;
+    // Every split must own at least one K tile: an empty split would store an accumulator no MMA wrote.
+    const int kt_per_split = (cp.k_tiles + kRouterSplits - 1) / kRouterSplits;
+    const int splits = (cp.k_tiles + kt_per_split - 1) / kt_per_split;
     SplitKSched<RouterCfg::BN> sc{};
     sc.m_tiles = (T + 127) / 128;
     sc.n_tiles = (E + RouterCfg::BN - 1) / RouterCfg::BN;
-    sc.splits = kRouterSplits;
-    sc.kt_per_split = (cp.k_tiles + kRouterSplits - 1) / kRouterSplits;
+    sc.splits = splits;
+    sc.kt_per_split = kt_per_split;
     sc.k_tiles = cp.k_tiles;
     sc.N = E;
     sc.b_row_tiles = (E + 127) / 128;
     RouterEpi e;
-    e.partial = w.partial;
+    e.partial = partial;
     e.split_stride = (long long)T * E;
     e.T = T;
     e.E = E;
@@ -725,7 +724,7 @@ extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, i
     const uint16_t* xn = norm ? static_cast<const uint16_t*>(x) : nullptr;
     const int epl = E / 32;
 #define NVFP4B_TOPK(EPL)                                                                                     \
-    router_topk_kernel<EPL><<<blocks, 256, 0, s>>>(w.partial, kRouterSplits, (long long)T * E, T, E, topk, xn, H, \
+    router_topk_kernel<EPL><<<blocks, 256, 0, s>>>(partial, splits, (long long)T * E, T, E, topk, xn, H, \
                                                    per_expert_scale, ids, weights)
     switch (epl) {
         case 1: NVFP4B_TOPK(1); break;
@@ -739,6 +738,27 @@ extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, i
     }
 #undef NVFP4B_TOPK
     return launch_status();
+}
+
+static int route_checks(const void* x, int T, int H, const void* proj, int E, int topk, const int* ids,
+                        const float* weights) {
+    if (!x || !proj || !ids || !weights) return NVFP4B_ERR_NULL;
+    if (T <= 0 || H <= 0 || (H % 64) || E <= 0 || (E % 32) || E > 256 || topk <= 0 || topk > 16 || topk > E)
+        return NVFP4B_ERR_SHAPE;
+    if (!aligned16(x) || !aligned16(proj)) return NVFP4B_ERR_ALIGN;
+    return NVFP4B_OK;
+}
+
+extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int topk,
+                                const float* per_expert_scale, int norm, int* ids, float* weights, void* workspace,
+                                void* stream) {
+    if (!workspace) return NVFP4B_ERR_NULL;
+    const int st = route_checks(x, T, H, proj, E, topk, ids, weights);
+    if (st) return st;
+    if (!aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    const Workspace w = carve(workspace, T, H, 32, E, topk);   // the router part of the layout ignores I
+    return route_launch(x, T, H, proj, E, topk, per_expert_scale, norm, ids, weights, w.partial,
+                        (cudaStream_t)stream);
 }
 
 static int moe_common_checks(const void* x, int T, const int* ids, const float* weights, int topk,
