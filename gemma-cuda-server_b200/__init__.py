@@ -24,7 +24,7 @@ _P = ctypes.c_void_p
 _lib = None
 
 STATUS = {0: "OK", -1: "ERR_SHAPE", -2: "ERR_ALIGN", -3: "ERR_NULL", -4: "ERR_CUDA", -5: "ERR_ARCH",
-          -6: "ERR_TIMEOUT", -7: "ERR_ARG"}
+          -6: "ERR_TIMEOUT", -7: "ERR_ARG", -8: "ERR_SCRATCH"}
 OUT_BF16_ROWMAJOR, OUT_F32_COLMAJOR, OUT_F32_ROWMAJOR = 0, 1, 2
 
 
@@ -216,6 +216,8 @@ def _moe_sigs():
         "nvfp4b_moe_max_rows": ([ctypes.c_int] * 3, ctypes.c_int),
         "nvfp4b_moe_route": ([_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P,
                               _P, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_route_noalloc": ([_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P,
+                                      ctypes.c_int, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_forward": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float, _P,
                                 _P, ctypes.c_int, _P, _P], ctypes.c_int),
         "nvfp4b_moe_calibrate": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float,
@@ -289,6 +291,18 @@ def moe_route(x, proj, topk: int, workspace, per_expert_scale=None, norm: bool =
     _check("moe_route", _moe_sigs().nvfp4b_moe_route(_ptr(x), T, H, _ptr(proj), E, topk, _ptr(per_expert_scale),
                                                       1 if norm else 0, _ptr(ids), _ptr(weights), _ptr(workspace),
                                                       _stream(stream)))
+    return ids, weights
+
+
+def moe_route_noalloc(x, proj, topk: int, ids, weights, per_expert_scale=None, norm: bool = False, stream=None):
+    """moe_route without a workspace: the library's fixed per-device scratch holds the partial logits (T * E must be
+    <= 262144).  ids/weights are caller-provided, so the call allocates nothing; calls that overlap in time on one
+    device must not be issued (they share the scratch)."""
+    T, H = x.shape
+    E = proj.shape[0]
+    _check("moe_route_noalloc", _moe_sigs().nvfp4b_moe_route_noalloc(
+        _ptr(x), T, H, _ptr(proj), E, topk, _ptr(per_expert_scale), 1 if norm else 0, _ptr(ids), _ptr(weights),
+        _stream(stream)))
     return ids, weights
 
 

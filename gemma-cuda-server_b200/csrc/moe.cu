@@ -26,6 +26,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "gemm_core.cuh"
 #include "sm100.cuh"
@@ -759,6 +761,52 @@ extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, i
     const Workspace w = carve(workspace, T, H, 32, E, topk);   // the router part of the layout ignores I
     return route_launch(x, T, H, proj, E, topk, per_expert_scale, norm, ids, weights, w.partial,
                         (cudaStream_t)stream);
+}
+
+// ---- Router with no caller workspace and no allocation ----------------------------------------------------------
+// For callers that cannot allocate or hand in scratch memory: a decode loop that reserves all of its device memory
+// once, up front (the reference's decode step does exactly that, src/forward.cu:394-409, because a per-step cudaMalloc
+// synchronises the device), and a host runtime whose memory planner owns every byte on the device.  Neither has a
+// workspace arena to pass to nvfp4b_moe_route.  This entry keeps the split-K partial logits in a file-scope device
+// array instead, so the call allocates nothing (no cudaMalloc/cudaFree, no library allocator).
+//
+// Limit: kRouteScratchBytes (4 MiB) of partials, i.e. kRouterSplits * T * E * 4 bytes: T * E <= 262144 (T <= 2048 at
+// E = 128).  Larger calls are rejected with NVFP4B_ERR_SCRATCH before anything is launched.
+// The array is one per device and per loaded library: calls that overlap in time on the same device (two streams,
+// or two host threads without ordering between their streams) race on it and produce wrong routes.
+constexpr size_t kRouteScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) float g_route_scratch[kRouteScratchBytes / sizeof(float)];
+
+// Device address of g_route_scratch on the current device.  The host-side symbol is not a device address, so it is
+// looked up with cudaGetSymbolAddress once per device, with that device current; the first call on a device also
+// loads the module there, so make it before any stream capture that should contain this entry.
+static float* route_scratch_ptr() {
+    static std::mutex mu;
+    static float* cached[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cached[dev]) {
+        void* p = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&p, g_route_scratch);
+        if (err != cudaSuccess) {
+            record_cuda_error(err);
+            return nullptr;
+        }
+        cached[dev] = static_cast<float*>(p);
+    }
+    return cached[dev];
+}
+
+extern "C" int nvfp4b_moe_route_noalloc(const void* x, int T, int H, const void* proj, int E, int topk,
+                                        const float* per_expert_scale, int norm, int* ids, float* weights,
+                                        void* stream) {
+    const int st = route_checks(x, T, H, proj, E, topk, ids, weights);
+    if (st) return st;
+    if ((size_t)kRouterSplits * (size_t)T * (size_t)E * sizeof(float) > kRouteScratchBytes) return NVFP4B_ERR_SCRATCH;
+    float* partial = route_scratch_ptr();
+    if (!partial) return NVFP4B_ERR_CUDA;
+    return route_launch(x, T, H, proj, E, topk, per_expert_scale, norm, ids, weights, partial, (cudaStream_t)stream);
 }
 
 static int moe_common_checks(const void* x, int T, const int* ids, const float* weights, int topk,

@@ -35,7 +35,8 @@ enum nvfp4b_status {
     NVFP4B_ERR_CUDA = -4,    /* a CUDA call failed; nvfp4b_last_cuda_error() has the cudaError_t */
     NVFP4B_ERR_ARCH = -5,    /* the current device is not an sm_100 part */
     NVFP4B_ERR_TIMEOUT = -6, /* a bounded device-side wait expired (no fault, the context stays usable) */
-    NVFP4B_ERR_ARG = -7      /* an enum/flag argument has an unknown value */
+    NVFP4B_ERR_ARG = -7,     /* an enum/flag argument has an unknown value */
+    NVFP4B_ERR_SCRATCH = -8  /* the problem needs more scratch than a fixed-size (no-allocation) entry point holds */
 };
 
 /* Library version string. */
@@ -140,6 +141,16 @@ int nvfp4b_moe_max_rows(int T, int E, int topk);
  * x [T, H] bf16, proj [E, H] bf16; E % 32 == 0, E <= 256, topk <= 16.  ids [T, topk] int32, weights fp32. */
 int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, int E, int topk, const float* per_expert_scale,
                      int norm, int* ids, float* weights, void* workspace, void* stream);
+
+/* nvfp4b_moe_route without a workspace argument; it allocates nothing.  No counterpart in the reference (whose router
+ * kernels, src/forward.cu:192-234, write into model-owned buffers): it serves callers that cannot allocate or pass
+ * scratch, e.g. a decode loop that reserves all of its memory up front.  The split-K partial logits live in a
+ * fixed 4 MiB device array inside the library, one per device: T * E must be <= 262144 (T <= 2048 at E = 128), larger
+ * calls return NVFP4B_ERR_SCRATCH.  Calls that overlap in time on one device race on that array: order them on one
+ * stream.  The first call on each device looks the array up (and loads the library's module there); make it before
+ * any stream capture that should contain this call.  Results equal nvfp4b_moe_route's. */
+int nvfp4b_moe_route_noalloc(const void* x, int T, int H, const void* proj, int E, int topk,
+                             const float* per_expert_scale, int norm, int* ids, float* weights, void* stream);
 
 /* Whole MoE layer: dispatch (counting sort of the T*topk assignments by expert, stable in token order),
  * quantisation of x fused into the dispatch scatter, grouped gate/up GEMM with the gelu_tanh(gate)*up epilogue
