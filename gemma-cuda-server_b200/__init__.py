@@ -184,7 +184,8 @@ def gemm(a, a_scales, a_dequant: float, b, b_scales, b_dequant: float, out: torc
 
 
 def set_gemm_tile_config(config: int) -> None:
-    """0 = automatic, 1 = 128x256 tiles (4 stages, one accumulator), 2 = 128x128 tiles (6 stages, two)."""
+    """0 = automatic, 1 = 128x256 tiles (4 stages, one accumulator), 2 = 128x128 tiles (6 stages, two),
+    3 = 256x256 tiles on a CTA pair (tcgen05 cta_group::2, 5 stages)."""
     _check("set_gemm_tile_config", lib().nvfp4b_gemm_set_tile_config(config))
 
 

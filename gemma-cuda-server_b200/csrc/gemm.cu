@@ -88,8 +88,9 @@ struct DenseEpi {
 
 using Tile256 = KCfg<256, 4, 1, 8>;
 using Tile128 = KCfg<128, 6, 2, 4>;
+using TilePair = PairCfg<5, 8>;
 
-int g_variant = 0;   // 0 = automatic, 1 = TILE_256, 2 = TILE_128
+int g_variant = 0;   // 0 = automatic, 1 = TILE_256, 2 = TILE_128, 3 = TILE_PAIR
 
 template <class C, int OUT>
 int run_dense(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, const GemmParams& p,
@@ -126,6 +127,52 @@ int run_dense(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uin
     return launch_core<C>(ma, mb, cp, s, e, grid, stream);
 }
 
+template <int OUT>
+int run_dense_pair(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, const GemmParams& p,
+                   cudaStream_t stream) {
+    using C = TilePair;
+    CUtensorMap ma, mb, msa, msb;
+    int st = make_kmajor_map(&ma, a, p.M, p.K / 2, C::BM);
+    if (st) return st;
+    st = make_kmajor_map(&mb, b, p.N, p.K / 2, C::BN / 2);
+    if (st) return st;
+    st = make_scale_map(&msa, a_sf, (long long)scale_bytes(p.M, p.K));
+    if (st) return st;
+    st = make_scale_map(&msb, b_sf, (long long)scale_bytes(p.N, p.K));
+    if (st) return st;
+    CoreParams cp;
+    cp.err = device_error_ptr();
+    if (!cp.err) return NVFP4B_ERR_CUDA;
+    cp.sfa = a_sf;
+    cp.sfb = b_sf;
+    cp.tile_cols = (p.K / 16 + 3) / 4;
+    cp.k_tiles = (cp.tile_cols + 3) / 4;
+    PairDenseSched s;
+    s.m_tiles = (p.M + C::PAIR_M - 1) / C::PAIR_M;
+    s.n_tiles = (p.N + C::BN - 1) / C::BN;
+    s.group_m = 8;
+    s.k_tiles = cp.k_tiles;
+    DenseEpi<OUT> e;
+    e.d = p.d;
+    e.ldd = p.ldd;
+    e.M = p.M;
+    e.N = p.N;
+    e.alpha = p.alpha;
+    e.b_dequant = p.b_dequant;
+    e.d_a_amax = p.d_a_amax;
+    return launch_pair<C>(ma, mb, msa, msb, cp, s, e, s.m_tiles * s.n_tiles, stream);
+}
+
+int dispatch_pair(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, const GemmParams& p,
+                  cudaStream_t stream) {
+    switch (p.out_kind) {
+        case NVFP4B_OUT_BF16_ROWMAJOR: return run_dense_pair<NVFP4B_OUT_BF16_ROWMAJOR>(a, a_sf, b, b_sf, p, stream);
+        case NVFP4B_OUT_F32_COLMAJOR: return run_dense_pair<NVFP4B_OUT_F32_COLMAJOR>(a, a_sf, b, b_sf, p, stream);
+        case NVFP4B_OUT_F32_ROWMAJOR: return run_dense_pair<NVFP4B_OUT_F32_ROWMAJOR>(a, a_sf, b, b_sf, p, stream);
+        default: return NVFP4B_ERR_ARG;
+    }
+}
+
 template <class C>
 int dispatch_out(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, const GemmParams& p,
                  cudaStream_t stream) {
@@ -140,19 +187,26 @@ int dispatch_out(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const 
 }  // namespace
 
 // 2-D K-major tensor map over `rows` rows of `row_bytes` bytes, box = 128 bytes x box_rows, 128-byte swizzle.
-int make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_rows) {
-    typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
     static EncodeTiledFn enc = nullptr;
     if (!enc) {
         void* ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess)
-            return record_cuda_error(cudaErrorNotSupported);
+            return nullptr;
         enc = reinterpret_cast<EncodeTiledFn>(ptr);
     }
+    return enc;
+}
+
+int make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return record_cuda_error(cudaErrorNotSupported);
     cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
     cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
@@ -163,9 +217,23 @@ int make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long lon
     return r == CUDA_SUCCESS ? NVFP4B_OK : NVFP4B_ERR_ALIGN;
 }
 
+int make_scale_map(CUtensorMap* map, const void* base, long long bytes) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return record_cuda_error(cudaErrorNotSupported);
+    cuuint64_t dims[2] = {256u, (cuuint64_t)(bytes / 256)};
+    cuuint64_t strides[1] = {256u};
+    cuuint32_t box[2] = {256u, 8u};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? NVFP4B_OK : NVFP4B_ERR_ALIGN;
+}
+
 int gemm_dense(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, GemmParams p,
                cudaStream_t stream) {
     const int v = g_variant != 0 ? g_variant : 1;
+    if (v == 3) return dispatch_pair(a, a_sf, b, b_sf, p, stream);
     if (v == 2) return dispatch_out<Tile128>(a, a_sf, b, b_sf, p, stream);
     return dispatch_out<Tile256>(a, a_sf, b, b_sf, p, stream);
 }
@@ -196,7 +264,7 @@ extern "C" int nvfp4b_gemm(const uint8_t* a, const uint8_t* a_scales, float a_de
 }
 
 extern "C" int nvfp4b_gemm_set_tile_config(int config) {
-    if (config < 0 || config > 2) return NVFP4B_ERR_ARG;
+    if (config < 0 || config > 3) return NVFP4B_ERR_ARG;
     g_variant = config;
     return NVFP4B_OK;
 }

@@ -454,7 +454,7 @@ struct DownEpi {
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
             const int lane = threadIdx.x & 31;
-            float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 2) * (32 * 33);
+            float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 4) * (32 * 33);   // epilogue warps are 4..
             const int sub = lane >> 3, q = (lane & 7) * 4;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {

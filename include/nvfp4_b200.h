@@ -89,7 +89,8 @@ int nvfp4b_gemm(const uint8_t* a, const uint8_t* a_scales, float a_dequant, cons
                 int M, int N, int K, void* d, int out_kind, long long ldd, void* stream);
 
 /* Selects the dense GEMM tile configuration for subsequent calls in this process: 0 = automatic (default),
- * 1 = 128x256 tiles, 4-stage pipeline, one TMEM accumulator; 2 = 128x128 tiles, 6 stages, two accumulators. */
+ * 1 = 128x256 tiles, 4-stage pipeline, one TMEM accumulator; 2 = 128x128 tiles, 6 stages, two accumulators;
+ * 3 = 256x256 tiles computed by a CTA pair (cluster of two, tcgen05 cta_group::2), 5 stages. */
 int nvfp4b_gemm_set_tile_config(int config);
 
 /* Reads the library's device-side error word (set by a kernel whose bounded wait expired, see

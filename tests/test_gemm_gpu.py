@@ -17,8 +17,17 @@ def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+@pytest.fixture(params=[1, 2, 3], ids=["tile256", "tile128", "pair"])
+def tile_config(request):
+    """Every dense tile configuration: 128x256 and 128x128 single-CTA tiles, 256x256 CTA-pair tiles."""
+    p = require_gpu()
+    p.set_gemm_tile_config(request.param)
+    yield request.param
+    p.set_gemm_tile_config(0)
+
+
 @pytest.mark.parametrize("tag", ["default", "ragged"])
-def test_reference_generator_cases_colmajor(golden, tag):
+def test_reference_generator_cases_colmajor(golden, tag, tile_config):
     """tests/test_fp4_gemm.cu flow: host-swizzled scales, nvfp4_gemm -> fp32 column-major D (ld = M)."""
     p = require_gpu()
     g = golden("gemm_cases.npz")
@@ -50,7 +59,7 @@ def _quantized_operands(M, N, K, seed):
 @pytest.mark.parametrize("M,N,K", [(16, 2048, 2048),                 # cfg0
                                    (128, 2816, 2816), (256, 8448, 2816), (128, 14336, 4096),   # cfg2 (reduced M)
                                    (1, 256, 64), (130, 200, 192), (77, 136, 96), (300, 384, 2048)])
-def test_gemm_bf16_vs_dequant_oracle(M, N, K):
+def test_gemm_bf16_vs_dequant_oracle(M, N, K, tile_config):
     p = require_gpu()
     _, _, (px, sx, gx), (pw, sw, gw) = _quantized_operands(M, N, K, seed=M + N + K)
     A, As = _dev(px), _dev(orc.swizzle_scales(sx, M, K))
@@ -63,7 +72,7 @@ def test_gemm_bf16_vs_dequant_oracle(M, N, K):
     assert ok, msg
 
 
-def test_gemm_fp32_rowmajor_and_dynamic_alpha():
+def test_gemm_fp32_rowmajor_and_dynamic_alpha(tile_config):
     """fp32 row-major output; activation dequant taken from a device amax (the dynamic-scale pipeline)."""
     p = require_gpu()
     M, N, K = 256, 384, 1024
@@ -79,7 +88,7 @@ def test_gemm_fp32_rowmajor_and_dynamic_alpha():
     assert ok, msg
 
 
-def test_gemm_full_size_cfg2_sampled_rows():
+def test_gemm_full_size_cfg2_sampled_rows(tile_config):
     """cfg2 at M=4096, (K, N) = (4096, 14336): full-size launch, oracle on 96 sampled rows."""
     p = require_gpu()
     M, N, K = 4096, 14336, 4096
