@@ -21,13 +21,54 @@ namespace nvfp4b {
 
 namespace {
 
-template <int OUT>
+// STAGED (bf16 row-major only): each epilogue warp turns its 32-row x 32-column chunks around in a 2 KB
+// shared-memory tile (16-byte segments XOR-swizzled by (row >> 1) & 3, conflict-free both ways) so every store
+// instruction writes 8 rows x 64 contiguous bytes -- whole sectors -- instead of 32 rows x 16 bytes.
+template <int OUT, bool STAGED = false>
 struct DenseEpi {
+    static constexpr int SMEM_PER_WARP = 2048;
     void* d;
     long long ldd;
     int M, N;
     float alpha, b_dequant;
     const float* d_a_amax;
+
+    __device__ __forceinline__ void store_staged(int row0, int n0, int lane, const uint32_t (&r)[32], float a,
+                                                 uint8_t* tile) const {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(a * __uint_as_float(r[8 * v + 2 * i]),
+                                                               a * __uint_as_float(r[8 * v + 2 * i + 1]));
+                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            *reinterpret_cast<uint4*>(tile + lane * 64 + ((v ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        __syncwarp();
+        const int seg = lane & 3;
+        const int col = n0 + 8 * seg;
+        const bool vec = n0 + 32 <= N && (ldd & 7) == 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int rr = 8 * i + (lane >> 2);
+            const uint4 val = *reinterpret_cast<const uint4*>(tile + rr * 64 + ((seg ^ ((rr >> 1) & 3)) << 4));
+            const long long m = (long long)row0 + rr;
+            if (m >= M) continue;
+            __nv_bfloat16* D = static_cast<__nv_bfloat16*>(d) + m * ldd + col;
+            if (vec) {
+                *reinterpret_cast<uint4*>(D) = val;
+            } else {
+                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&val);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    if (col + e < N) D[e] = h[e];
+            }
+        }
+        __syncwarp();
+    }
 
     __device__ __forceinline__ void store(long long m, int n0, const uint32_t (&r)[32], float a) const {
         if constexpr (OUT == NVFP4B_OUT_BF16_ROWMAJOR) {
@@ -74,10 +115,22 @@ struct DenseEpi {
 
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
-                                            uint8_t*) const {
+                                            uint8_t* esm) const {
+        const float a = d_a_amax ? __fdiv_rn(b_dequant, gscale_from_amax(__ldg(d_a_amax))) : alpha;
+        if constexpr (STAGED && OUT == NVFP4B_OUT_BF16_ROWMAJOR) {
+            const int lane = threadIdx.x & 31;
+            uint8_t* tile = esm + ((threadIdx.x >> 5) - 4) * SMEM_PER_WARP;   // epilogue warps are 4..
+            const int row0 = ti.a_row + row - lane;
+            if (row0 >= M) return;                                            // warp-uniform
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int n0 = ti.n0 + col_base + 32 * c;                    // warp-uniform
+                if (n0 < N) store_staged(row0, n0, lane, r[c], a, tile);
+            }
+            return;
+        }
         const long long m = (long long)ti.a_row + row;
         if (m >= M) return;
-        const float a = d_a_amax ? __fdiv_rn(b_dequant, gscale_from_amax(__ldg(d_a_amax))) : alpha;
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
             const int n0 = ti.n0 + col_base + 32 * c;
@@ -88,7 +141,7 @@ struct DenseEpi {
 
 using Tile256 = KCfg<256, 4, 1, 8>;
 using Tile128 = KCfg<128, 6, 2, 4>;
-using TilePair = PairCfg<5, 8>;
+using TilePair = PairCfg<5, 8, 8 * 2048>;   // + staging tiles of the bf16 store epilogue
 
 int g_variant = 0;   // 0 = automatic, 1 = TILE_256, 2 = TILE_128, 3 = TILE_PAIR
 
@@ -152,7 +205,7 @@ int run_dense_pair(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, cons
     s.n_tiles = (p.N + C::BN - 1) / C::BN;
     s.group_m = 8;
     s.k_tiles = cp.k_tiles;
-    DenseEpi<OUT> e;
+    DenseEpi<OUT, true> e;
     e.d = p.d;
     e.ldd = p.ldd;
     e.M = p.M;
@@ -232,7 +285,9 @@ int make_scale_map(CUtensorMap* map, const void* base, long long bytes) {
 
 int gemm_dense(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, GemmParams p,
                cudaStream_t stream) {
-    const int v = g_variant != 0 ? g_variant : 1;
+    // Automatic: the CTA-pair tiles whenever there are more rows than one 128-row block (they halve each SM's
+    // operand traffic and stage the output through shared memory); 128 x 256 single-CTA tiles otherwise.
+    const int v = g_variant != 0 ? g_variant : (p.M > 128 ? 3 : 1);
     if (v == 3) return dispatch_pair(a, a_sf, b, b_sf, p, stream);
     if (v == 2) return dispatch_out<Tile128>(a, a_sf, b, b_sf, p, stream);
     return dispatch_out<Tile256>(a, a_sf, b, b_sf, p, stream);

@@ -7,11 +7,11 @@
 //                     (128 rows) and of B (BN rows), both 128-byte swizzled, plus 1-D bulk loads of the scale tiles
 //                     (the tile layout puts the scales of 128 rows x 256 K into 2 KB of contiguous memory).
 //   warp 1            TMEM owner and MMA issuer (one elected thread): four 128 x N x 64 MMAs per K-tile reading
-//                     their scales from a TMEM scale slot; tcgen05.commit releases the smem stage and the slot, and
+//                     their scales from the TMEM scale slot of the stage; tcgen05.commit releases the smem stage, and
 //                     a commit per output tile hands the accumulator to the epilogue.
 //   warps 2, 3        scale copiers: tcgen05.cp 32x128b.warpx4 moves each 512-byte scale tile (32 rows x 16 bytes)
 //                     into 4 TMEM columns, replicated over the four lane quadrants as the MMA reads them.  The copies
-//                     are issued apart from the MMAs, split over two threads, into rotating slots (one per K-tile):
+//                     are issued apart from the MMAs, split over two threads, into one TMEM slot per smem stage:
 //                     a tcgen05.cp costs the tensor pipe tens of cycles, and issued in line with the MMAs the 12
 //                     copies of a 128 x 256 K-tile nearly doubled its time.
 //   warps 4..         epilogue (EPI_WARPS warps): warp w reads TMEM lane quadrant w % 4; with 8 warps each quadrant
@@ -35,12 +35,9 @@ namespace nvfp4b {
 // of 128 bytes is four MMAs and the shared-memory descriptors advance by 32 bytes per MMA.
 enum class Kind { NVF4, BF16 };
 
-// TMEM scale slots: the scale copies of K-tile g go to slot g % SF_SLOTS, so the copier warps can run up to
-// SF_SLOTS - 1 K-tiles ahead of the MMAs that read them (at most 4; 1 when there are no scales).
-constexpr int sf_slots(int free_cols, int cols_per_slot) {
-    return cols_per_slot == 0 ? 1 : (free_cols / cols_per_slot >= 4 ? 4 : free_cols / cols_per_slot);
-}
-
+// TMEM scale slots: one per smem stage.  The copier warps fill slot s from stage s as soon as the stage's loads
+// land, so they run ahead of the MMAs by up to STAGES - 1 K-tiles; a slot is free again when its stage is (the
+// producer refills stage s only after the MMAs that read slot s completed), so no separate release is needed.
 template <int BN_, int STAGES_, int ACC_BUFS_, int EPI_WARPS_, Kind KIND_ = Kind::NVF4, int EPI_SMEM_ = 0>
 struct KCfg {
     static constexpr int EPI_SMEM = EPI_SMEM_;           // extra shared memory handed to the epilogue policy
@@ -58,10 +55,10 @@ struct KCfg {
     static constexpr int SF_COLS_A = SCALED ? 16 : 0, SF_COLS_B = SCALED ? 4 * (BN / 32) : 0;
     static constexpr int SF_COL0 = ACC_BUFS * BN;
     static constexpr int TMEM_COLS = 512;
-    static constexpr int SF_SLOTS = sf_slots(TMEM_COLS - SF_COL0, SF_COLS_A + SF_COLS_B);
+    static constexpr int SF_SLOTS = STAGES;
     static constexpr int COLS_PER_WARP = BN * 4 / EPI_WARPS;
     static constexpr int CHUNKS = COLS_PER_WARP / 32;
-    static constexpr int BAR_BYTES = ((2 * STAGES + 2 * ACC_BUFS + 2 * SF_SLOTS) * 8 + 16 + 127) / 128 * 128;
+    static constexpr int BAR_BYTES = ((3 * STAGES + 2 * ACC_BUFS) * 8 + 16 + 127) / 128 * 128;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_SMEM + 1024;
     static_assert(SF_COL0 + SF_SLOTS * (SF_COLS_A + SF_COLS_B) <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -238,9 +235,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + C::ACC_BUFS;
-    uint64_t* sf_full = tempty + C::ACC_BUFS;
-    uint64_t* sf_free = sf_full + C::SF_SLOTS;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + C::SF_SLOTS);
+    uint64_t* sf_full = tempty + C::ACC_BUFS;     // per stage: its scales are in TMEM slot `stage`
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + C::STAGES);
     volatile int* sflag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint8_t* esm = sSFB + C::STAGES * C::SFB_BYTES + C::BAR_BYTES;   // 128-byte aligned epilogue scratch
 
@@ -248,7 +244,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < C::ACC_BUFS; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 32 * C::EPI_WARPS); }
-        for (int b = 0; b < C::SF_SLOTS; ++b) { mbar_init(&sf_full[b], 2); mbar_init(&sf_free[b], 1); }
+        for (int b = 0; b < C::STAGES; ++b) mbar_init(&sf_full[b], 2);
         *sflag = 0;
         fence_mbar_init();
     }
@@ -293,7 +289,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            int stage = 0, abuf = 0, g = 0;
+            int stage = 0, abuf = 0;
             uint32_t phase = 0, aphase = 0;
             bool ok = true;
             const uint32_t sfa_col = tmem + (uint32_t)C::SF_COL0;
@@ -314,19 +310,13 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     const uint32_t sfb_base = smem_u32(sSFB + stage * C::SFB_BYTES);
                     const uint32_t acc0 = kt != ti.kt0 ? 1u : 0u;
                     if constexpr (C::SCALED) {
-                        const int slot = g % C::SF_SLOTS;
-                        if (!mbar_wait(&sf_full[slot], (uint32_t)((g / C::SF_SLOTS) & 1), sflag, kErrTimeoutMma)) {
-                            ok = false;
-                            break;
-                        }
+                        if (!mbar_wait(&sf_full[stage], phase, sflag, kErrTimeoutMma)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t so = (uint32_t)(slot * (C::SF_COLS_A + C::SF_COLS_B));
+                        const uint32_t so = (uint32_t)(stage * (C::SF_COLS_A + C::SF_COLS_B));
                         for (int j = 0; j < nks; ++j)
                             mma_nvf4(d_tmem, desc_kmajor_sw128(a_base + 32 * j), desc_kmajor_sw128(b_base + 32 * j),
                                      idesc, sfa_col + so + 4 * j, sfb_col + so + (C::BN / 32) * j,
                                      (acc0 | j) != 0 ? 1u : 0u);
-                        tc_commit(&sf_free[slot]);
-                        ++g;
                     } else {
                         for (int j = 0; j < nks; ++j)
                             mma_bf16(d_tmem, desc_kmajor_sw128(a_base + 32 * j), desc_kmajor_sw128(b_base + 32 * j),
@@ -344,7 +334,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         // ---------------- scale copier (warps 2, 3) ----------------
         if (C::SCALED && lane == 0) {
             const int part = warp - 2;
-            int stage = 0, g = 0;
+            int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             const uint32_t sfa_col = tmem + (uint32_t)C::SF_COL0;
@@ -352,19 +342,13 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const TileInfo ti = sched.tile(t);
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    const int slot = g % C::SF_SLOTS;
-                    if (!mbar_wait(&full[stage], phase, sflag, kErrTimeoutMma) ||
-                        !mbar_wait(&sf_free[slot], (uint32_t)(((g / C::SF_SLOTS) & 1) ^ 1), sflag, kErrTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
+                    if (!mbar_wait(&full[stage], phase, sflag, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t so = (uint32_t)(slot * (C::SF_COLS_A + C::SF_COLS_B));
+                    const uint32_t so = (uint32_t)(stage * (C::SF_COLS_A + C::SF_COLS_B));
                     issue_scale_copies<C, false>(part, min(4, cp.tile_cols - kt * 4), sfa_col + so, sfb_col + so,
                                                  smem_u32(sSFA + stage * C::SFA_BYTES),
                                                  smem_u32(sSFB + stage * C::SFB_BYTES));
-                    tc_commit(&sf_full[slot]);
-                    ++g;
+                    tc_commit(&sf_full[stage]);
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
@@ -417,7 +401,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 //                     (tensor loads with cta_group::2; the leader posts the byte count of both CTAs).
 //   warp 1 (leader)   MMAs for the pair; commits release the stage in both CTAs and hand the accumulator to both
 //                     CTAs' epilogues.  (warp 1 of the peer only allocates TMEM.)
-//   warps 2-3 (leader) scale copies for the pair (cta_group::2), into rotating TMEM scale slots.
+//   warps 2-3 (leader) scale copies for the pair (cta_group::2), into one TMEM scale slot per smem stage.
 //   warps 4.. (both)  epilogue of the CTA's 128 rows; one arrival per warp on the leader's accumulator-empty barrier.
 template <int STAGES_, int EPI_WARPS_, int EPI_SMEM_ = 0>
 struct PairCfg {
@@ -434,10 +418,10 @@ struct PairCfg {
     static constexpr uint32_t PAIR_TX = 2u * STAGE_BYTES;     // bytes the leader's full barrier waits for
     static constexpr int SF_COLS_A = 16, SF_COLS_B = 32, SF_COL0 = BN;
     static constexpr int TMEM_COLS = 512;
-    static constexpr int SF_SLOTS = sf_slots(TMEM_COLS - SF_COL0, SF_COLS_A + SF_COLS_B);
+    static constexpr int SF_SLOTS = STAGES;
     static constexpr int COLS_PER_WARP = BN * 4 / EPI_WARPS;
     static constexpr int CHUNKS = COLS_PER_WARP / 32;
-    static constexpr int BAR_BYTES = ((2 * STAGES + 2 + 2 * SF_SLOTS) * 8 + 16 + 127) / 128 * 128;
+    static constexpr int BAR_BYTES = ((3 * STAGES + 2) * 8 + 16 + 127) / 128 * 128;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_SMEM + 1024;
     static_assert(SF_COL0 + SF_SLOTS * (SF_COLS_A + SF_COLS_B) <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -486,9 +470,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     uint64_t* empty = full + C::STAGES;
     uint64_t* tfull = empty + C::STAGES;
     uint64_t* tempty = tfull + 1;
-    uint64_t* sf_full = tempty + 1;
-    uint64_t* sf_free = sf_full + C::SF_SLOTS;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_free + C::SF_SLOTS);
+    uint64_t* sf_full = tempty + 1;               // per stage: its scales are in TMEM slot `stage`
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + C::STAGES);
     volatile int* sflag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     uint8_t* esm = sSFB + C::STAGES * C::SFB_BYTES + C::BAR_BYTES;
 
@@ -498,7 +481,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(tfull, 1);
         mbar_init(tempty, 2 * C::EPI_WARPS);
-        for (int b = 0; b < C::SF_SLOTS; ++b) { mbar_init(&sf_full[b], 2); mbar_init(&sf_free[b], 1); }
+        for (int b = 0; b < C::STAGES; ++b) mbar_init(&sf_full[b], 2);
         *sflag = 0;
         fence_mbar_init();
     }
@@ -552,7 +535,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader only) ----------------
         if (rank == 0 && lane == 0) {
-            int stage = 0, g = 0;
+            int stage = 0;
             uint32_t phase = 0, aphase = 0;
             bool ok = true;
             const uint32_t sfa_col = tmem + (uint32_t)C::SF_COL0;
@@ -570,21 +553,15 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     const uint32_t a_base = smem_u32(sA + stage * C::A_BYTES);
                     const uint32_t b_base = smem_u32(sB + stage * C::B_BYTES);
                     const uint32_t acc0 = kt != ti.kt0 ? 1u : 0u;
-                    const int slot = g % C::SF_SLOTS;
-                    if (!mbar_wait(&sf_full[slot], (uint32_t)((g / C::SF_SLOTS) & 1), sflag, kErrTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
+                    if (!mbar_wait(&sf_full[stage], phase, sflag, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t so = (uint32_t)(slot * (C::SF_COLS_A + C::SF_COLS_B));
+                    const uint32_t so = (uint32_t)(stage * (C::SF_COLS_A + C::SF_COLS_B));
                     for (int j = 0; j < nks; ++j)
                         mma_nvf4_pair(tmem, desc_kmajor_sw128(a_base + 32 * j), desc_kmajor_sw128(b_base + 32 * j),
                                       idesc, sfa_col + so + 4 * j, sfb_col + so + 8 * j, (acc0 | j) != 0 ? 1u : 0u);
                     const uint32_t eb = smem_u32(&empty[stage]);
                     tc_commit_pair(eb);
                     tc_commit_pair(mapa_shared(eb, 1));
-                    tc_commit_pair(smem_u32(&sf_free[slot]));
-                    ++g;
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
@@ -597,7 +574,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         // ---------------- scale copiers (leader warps 2, 3) ----------------
         if (rank == 0 && lane == 0) {
             const int part = warp - 2;
-            int stage = 0, g = 0;
+            int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             const uint32_t sfa_col = tmem + (uint32_t)C::SF_COL0;
@@ -605,19 +582,13 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             for (int t = cluster; t < num_tiles && ok; t += clusters) {
                 const TileInfo ti = sched.tile(t);
                 for (int kt = ti.kt0; kt < ti.kt1; ++kt) {
-                    const int slot = g % C::SF_SLOTS;
-                    if (!mbar_wait(&full[stage], phase, sflag, kErrTimeoutMma) ||
-                        !mbar_wait(&sf_free[slot], (uint32_t)(((g / C::SF_SLOTS) & 1) ^ 1), sflag, kErrTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
+                    if (!mbar_wait(&full[stage], phase, sflag, kErrTimeoutMma)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t so = (uint32_t)(slot * (C::SF_COLS_A + C::SF_COLS_B));
+                    const uint32_t so = (uint32_t)(stage * (C::SF_COLS_A + C::SF_COLS_B));
                     issue_scale_copies<C, true>(part, min(4, cp.tile_cols - kt * 4), sfa_col + so, sfb_col + so,
                                                 smem_u32(sSFA + stage * C::SFA_BYTES),
                                                 smem_u32(sSFB + stage * C::SFB_BYTES));
-                    tc_commit_pair(smem_u32(&sf_full[slot]));
-                    ++g;
+                    tc_commit_pair(smem_u32(&sf_full[stage]));
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
