@@ -534,7 +534,8 @@ def main():
         achieved = W.units_per_step / kern_s / 1e12
         fp4_peak = peaks["bf16_tflops"] * 4.0
         roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": achieved / fp4_peak, "traffic": NCU_TRAFFIC["gemm"], "kernel": "gemm_nvf4_kernel",
+                "frac": achieved / fp4_peak, "traffic": NCU_TRAFFIC["gemm"],
+                "kernel": "nvf4_gemm_pair_kernel (256x256 tiles on a CTA pair, tcgen05 cta_group::2)",
                 "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4"}
 
     cpu = None

@@ -24,9 +24,10 @@ namespace {
 // STAGED (bf16 row-major only): each epilogue warp turns its 32-row x 32-column chunks around in a 2 KB
 // shared-memory tile (16-byte segments XOR-swizzled by (row >> 1) & 3, conflict-free both ways) so every store
 // instruction writes 8 rows x 64 contiguous bytes -- whole sectors -- instead of 32 rows x 16 bytes.
+constexpr int kStoreTileBytes = 2048;   // per epilogue warp: one 32 x 32 bf16 tile
+
 template <int OUT, bool STAGED = false>
 struct DenseEpi {
-    static constexpr int SMEM_PER_WARP = 2048;
     void* d;
     long long ldd;
     int M, N;
@@ -119,7 +120,7 @@ struct DenseEpi {
         const float a = d_a_amax ? __fdiv_rn(b_dequant, gscale_from_amax(__ldg(d_a_amax))) : alpha;
         if constexpr (STAGED && OUT == NVFP4B_OUT_BF16_ROWMAJOR) {
             const int lane = threadIdx.x & 31;
-            uint8_t* tile = esm + ((threadIdx.x >> 5) - 4) * SMEM_PER_WARP;   // epilogue warps are 4..
+            uint8_t* tile = esm + ((threadIdx.x >> 5) - 4) * kStoreTileBytes;   // epilogue warps are 4..
             const int row0 = ti.a_row + row - lane;
             if (row0 >= M) return;                                            // warp-uniform
 #pragma unroll
@@ -141,7 +142,7 @@ struct DenseEpi {
 
 using Tile256 = KCfg<256, 4, 1, 8>;
 using Tile128 = KCfg<128, 6, 2, 4>;
-using TilePair = PairCfg<5, 8, 8 * 2048>;   // + staging tiles of the bf16 store epilogue
+using TilePair = PairCfg<5, 8, 8 * kStoreTileBytes>;   // + bf16 store staging tiles
 
 int g_variant = 0;   // 0 = automatic, 1 = TILE_256, 2 = TILE_128, 3 = TILE_PAIR
 

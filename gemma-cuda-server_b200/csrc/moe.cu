@@ -24,6 +24,7 @@
 //                 it slower at these sizes).
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -57,7 +58,7 @@ struct Workspace {
     int* row_token;
     float* row_weight;
     int* row_assign;
-    float* y;             // [T*topk, H] fp32 weighted expert outputs, assignment-major (deterministic combine)
+    uint16_t* y;          // [T*topk, H] fp16 weighted expert outputs, assignment-major (deterministic combine)
     uint8_t* a_codes;
     uint8_t* a_scales;
     uint8_t* h_codes;
@@ -84,7 +85,7 @@ Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     w.row_token = (int*)take((size_t)rows * 4);
     w.row_weight = (float*)take((size_t)rows * 4);
     w.row_assign = (int*)take((size_t)rows * 4);
-    w.y = (float*)take((size_t)n_assign * H * 4);
+    w.y = (uint16_t*)take((size_t)n_assign * H * 2);
     w.a_codes = (uint8_t*)take((size_t)rows * (H / 2));
     w.a_scales = (uint8_t*)take(scale_bytes(rows, H));
     w.h_codes = (uint8_t*)take((size_t)rows * (I / 2));
@@ -425,15 +426,28 @@ struct GateUpEpi {
     }
 };
 
+// f32 pair -> f16x2 (round to nearest, saturating to +-65504 instead of overflowing), lo in the low half.
+__device__ __forceinline__ uint32_t pack_half2_sat(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ float2 unpack_half2(uint32_t v) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+
 // Down epilogue.  Row m holds assignment a = token * topk + slot (or -1 for padding); its contribution is
 // weight(a) / (g_h * g_w2) * acc.
-//   DETERMINISTIC = true (default): stores the fp32 row into y[a, :] (assignment-major); moe_combine_kernel then
-//     sums each token's topk rows in slot order, giving bit-reproducible output.
-//   DETERMINISTIC = false: adds the row into out[token, :] with 16-byte fp32 vector reductions (order-dependent
+//   DETERMINISTIC = true (default): stores the row into y[a, :] (assignment-major) as fp16; moe_combine_kernel then
+//     sums each token's topk rows in slot order in fp32, giving bit-reproducible output.  fp16 (11-bit significand,
+//     relative rounding 2^-11) halves the bytes of the y round trip through HBM, which bounds this stage: y is
+//     T * topk * H values (92M for the 4096-token layer), written here and read back once by the combine.
+//   DETERMINISTIC = false: adds the fp32 row into out[token, :] with 16-byte vector reductions (order-dependent
 //     rounding; bounded by the L2's atomic throughput, so slower at large T*topk).
 template <bool DETERMINISTIC>
 struct DownEpi {
-    float* y;
+    uint16_t* y;
     float* out;
     int H, topk;
     const int* row_assign;
@@ -444,7 +458,7 @@ struct DownEpi {
     __device__ __forceinline__ void finish() const {}
 
     // DETERMINISTIC: each warp transposes its 32-row x 32-column chunk through shared memory (32 x 33 floats) so
-    // every store instruction writes four full 128-byte row segments of y instead of 32 scattered 16-byte pieces.
+    // every store instruction writes four full 64-byte row segments of y instead of 32 scattered 8-byte pieces.
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
                                             uint8_t* esm) const {
@@ -470,8 +484,8 @@ struct DownEpi {
                     const int ai = __shfl_sync(0xFFFFFFFFu, a, i);
                     const float* src = tile + i * 33 + q;
                     if (ai >= 0)
-                        *reinterpret_cast<float4*>(y + (long long)ai * H + n0 + q) =
-                            make_float4(src[0], src[1], src[2], src[3]);
+                        *reinterpret_cast<uint2*>(y + (long long)ai * H + n0 + q) =
+                            make_uint2(pack_half2_sat(src[0], src[1]), pack_half2_sat(src[2], src[3]));
                 }
             }
         } else {
@@ -491,21 +505,32 @@ struct DownEpi {
     }
 };
 
-// out[t] (+)= sum_j y[t*k + j] over the k slots in order, fp32.  One warp per token, 4 columns per lane step.
-__global__ void __launch_bounds__(256) moe_combine_kernel(const float* __restrict__ y, int T, int H, int topk,
+// out[t] (+)= sum_j y[t*k + j] over the k slots in order, fp32 accumulation of the fp16 rows.  One warp per token,
+// 8 columns (16 bytes of y) per lane step; H % 256 == 0.
+__global__ void __launch_bounds__(256) moe_combine_kernel(const uint16_t* __restrict__ y, int T, int H, int topk,
                                                           float* __restrict__ out, int accumulate) {
     const int lane = threadIdx.x & 31;
     const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     if (t >= T) return;
-    const float* src = y + (long long)t * topk * H;
+    const uint16_t* src = y + (long long)t * topk * H;
     float* dst = out + (long long)t * H;
-    for (int c = lane * 4; c < H; c += 128) {
-        float4 acc = accumulate ? *reinterpret_cast<const float4*>(dst + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j = 0; j < topk; ++j) {
-            const float4 q = __ldg(reinterpret_cast<const float4*>(src + (long long)j * H + c));
-            acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+    for (int c = lane * 8; c < H; c += 256) {
+        float acc[8];
+        if (accumulate) {
+            const float4 u = *reinterpret_cast<const float4*>(dst + c), v = *reinterpret_cast<const float4*>(dst + c + 4);
+            acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
         }
-        *reinterpret_cast<float4*>(dst + c) = acc;
+        for (int j = 0; j < topk; ++j) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + (long long)j * H + c));
+            const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
+            acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+            acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+        }
+        *reinterpret_cast<float4*>(dst + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(dst + c + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 

@@ -155,14 +155,15 @@ int nvfp4b_moe_route_noalloc(const void* x, int T, int H, const void* proj, int 
 
 /* Whole MoE layer: dispatch (counting sort of the T*topk assignments by expert, stable in token order),
  * quantisation of x fused into the dispatch scatter, grouped gate/up GEMM with the gelu_tanh(gate)*up epilogue
- * requantised to NVFP4, grouped down GEMM whose epilogue scales each row by its router weight into an fp32 row
- * buffer, and a combine summing each token's topk rows in slot order into out[t] (fp32 [T, H]; bit-reproducible).
- * flags: NVFP4B_MOE_* (ACCUMULATE adds onto out, e.g. the residual; ATOMIC uses fp32 atomic adds instead).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale:
- * in_gscale, or 2688 / max(*d_in_amax, 1e-9) on the device if d_in_amax is not NULL. */
+ * requantised to NVFP4, grouped down GEMM whose epilogue scales each row by its router weight into an fp16 row
+ * buffer, and a combine summing each token's topk rows in slot order in fp32 into out[t] (fp32 [T, H];
+ * bit-reproducible).  flags: NVFP4B_MOE_* (ACCUMULATE adds onto out, e.g. the residual; ATOMIC uses fp32 atomic
+ * adds instead).  ids/weights come from nvfp4b_moe_route or the caller.  Activation global scale: in_gscale, or
+ * 2688 / max(*d_in_amax, 1e-9) on the device if d_in_amax is not NULL. */
 enum nvfp4b_moe_flags {
     NVFP4B_MOE_ACCUMULATE = 1,  /* add the layer output onto out instead of overwriting it */
     NVFP4B_MOE_ATOMIC = 2       /* fp32 atomic adds into out instead of the (default, bit-reproducible) slot-ordered
-                                   combine over an fp32 row buffer */
+                                   combine over an fp16 row buffer */
 };
 int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
                        const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
@@ -195,7 +196,7 @@ typedef struct nvfp4b_moe_view {
     int* row_token;        /* [max_rows] token of each row, -1 for padding */
     float* row_weight;     /* [max_rows] router weight of each row */
     int* row_assign;       /* [max_rows] assignment (token * topk + slot) of each row, -1 for padding */
-    float* y;              /* [T*topk, H] fp32 weighted expert outputs, assignment-major */
+    uint16_t* y;           /* [T*topk, H] fp16 (IEEE binary16) weighted expert outputs, assignment-major */
     int* dest;             /* [T*topk] row of each (token, slot) */
     uint8_t* a_codes;      /* [max_rows, H/2] quantised x, expert-sorted */
     uint8_t* a_scales;

@@ -189,7 +189,8 @@ def test_accumulate_and_combine_modes(atomic):
     y2 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]), atomic=not atomic)
     torch.cuda.synchronize()
     assert torch.allclose(y1, base + y0, rtol=1e-5, atol=1e-5)
-    assert torch.allclose(y0, y2, rtol=1e-5, atol=1e-6)          # the two combine modes agree
+    # the two combine modes agree up to the fp16 rounding of the deterministic mode's row buffer (2^-11 relative)
+    assert torch.allclose(y0, y2, rtol=2e-3, atol=2e-3 * y2.abs().max().item())
     if not atomic:                                                 # the default combine is bit-reproducible
         y3 = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]))
         torch.cuda.synchronize()
