@@ -1,6 +1,7 @@
 // common.cuh -- shared device/host helpers for the sm_100a NVFP4 library.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -204,10 +205,41 @@ __device__ __forceinline__ uint32_t quantize16(const float* v, float g, uint32_t
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// Replaces, in the code word `c` of 8 elements (4 words of bf16 pairs), every nibble flagged in `diff` by the
-// exact float64 code.  Only flagged elements are recomputed; the word is picked with compile-time compares so the
-// inputs stay in registers.  With bf16 data and g = 2688/amax the quotient x*g/e4m3 is a ratio of small integers,
-// so a few percent of blocks hold an element within fp32 rounding of a midpoint.
+// Magnitude of an e2m1 code 0..7: 0, 0.5, 1, 1.5, 2, 3, 4, 6.
+__device__ __forceinline__ float e2m1_magnitude(uint32_t mag) {
+    if (mag < 2u) return 0.5f * (float)mag;
+    return __int_as_float((int)(((mag >> 1) - 1u + 127u) << 23)) * (1.0f + 0.5f * (float)(mag & 1u));
+}
+
+// Code of one element whose two bracket estimates straddle an e2m1 rounding boundary: the bracket codes are
+// magnitudes mh - 1 and mh, so the only question is which side of the boundary b between them the reference's
+// float64 quotient y = |x| / (stored / g) falls.  |x| * g (a bf16 times an fp32) differs from b * stored (exact in
+// fp32) by at least 2^-32 relative unless the two are equal, far more than float64 rounding can move y, so the
+// exact sign of |x| * g - b * stored decides -- taken in fp32 as (p - b*stored) + fma(|x|, g, -p) with p = fl(|x|*g)
+// (Sterbenz: the difference is exact, the sum has the exact sign).  Only an exact tie repeats the reference's
+// float64 arithmetic, where the rounding of y decides (ties go to the smaller magnitude).
+__device__ __forceinline__ uint32_t e2m1_resolve(float x, uint32_t code_hi, const BlockParams& p) {
+    const uint32_t mh = code_hi & 7u, ml = mh - 1u;
+    const float b = 0.5f * (e2m1_magnitude(ml) + e2m1_magnitude(mh));
+    const float ax = fabsf(x);
+    float d;
+    if (p.stored > 0.0f) {
+        const float pr = ax * p.g;
+        d = (pr - b * p.stored) + fmaf(ax, p.g, -pr);
+    } else {
+        d = ax - b;                                   // zero scale: L = 1
+    }
+    uint32_t mag = d > 0.0f ? mh : ml;
+    if (__builtin_expect(d == 0.0f && p.stored > 0.0f, 0)) {
+        const double L = __ddiv_rn((double)p.stored, (double)p.g);
+        mag = __ddiv_rn((double)ax, L) > (double)b ? mh : ml;
+    }
+    return mag | (code_hi & 8u);
+}
+
+// Replaces, in the code word `c` of 8 elements (4 words of bf16 pairs), every nibble flagged in `diff` by its
+// exact code (e2m1_resolve).  The word is picked with compile-time compares so the inputs stay in registers.  With
+// bf16 data and g = 2688/amax a few percent of blocks hold an element within 2^-20 of a rounding boundary.
 __device__ __forceinline__ uint32_t resolve_codes(uint32_t c, uint32_t diff, uint32_t w0, uint32_t w1, uint32_t w2,
                                                   uint32_t w3, const BlockParams& p) {
     while (diff) {
@@ -219,27 +251,61 @@ __device__ __forceinline__ uint32_t resolve_codes(uint32_t c, uint32_t diff, uin
         wi = j == 2 ? w2 : wi;
         wi = j == 3 ? w3 : wi;
         const float x = (i & 1) ? bf16hi(wi) : bf16lo(wi);
-        c = (c & ~(0xFu << (4 * i))) | (e2m1_code_exact(x, p.stored, p.g) << (4 * i));
+        c = (c & ~(0xFu << (4 * i))) | (e2m1_resolve(x, (c >> (4 * i)) & 0xFu, p) << (4 * i));
     }
     return c;
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Value of a positive e4m3 byte (b < 0x7F) by the hardware conversion e4m3 -> f16 (exact: every e4m3 value,
+// subnormals included, is an f16) -> f32.  The byte is fed to both halves of the pair, so lane order is moot.
+__device__ __forceinline__ float e4m3_value(uint32_t b) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((unsigned short)(b | (b << 8))));
+    return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+
 // Quantise one 16-element block given as 8 words of bf16 pairs (element 0 in the low half): returns the scale byte
-// and the 8 code bytes (element 0 in the low nibble of c0).  Straight-line: both bracket estimates of all 16 codes
-// are formed first and compared once; a block with any element near a rounding boundary is recomputed exactly.
+// and the 8 code bytes (element 0 in the low nibble of c0).  Fast path: the two bracket estimates of every code are
+// x * (g / stored) * (1 -/+ 2^-20), formed as one FFMA2 per pair and bracket with multipliers folded per block
+// (g / stored from rcp.approx: with the products it stays within 2^-22 of the exact quotient, well inside the
+// 2^-20 bracket).  Equal codes from both brackets are the reference's codes; a block with any element whose
+// brackets differ is finished by the float64 path for those elements only.
 __device__ __forceinline__ uint32_t quantize16_bf16(const uint32_t (&w)[8], float g, uint32_t& c0, uint32_t& c1) {
-    uint32_t m = 0;
+    float f[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
-    m = max(m & 0xFFFFu, m >> 16);
-    const BlockParams p = block_params(__uint_as_float(m << 16), g);
+    for (int i = 0; i < 8; ++i) {
+        f[2 * i] = bf16lo(w[i]);
+        f[2 * i + 1] = bf16hi(w[i]);
+    }
+    float bamax = fabsf(f[0]);
+#pragma unroll
+    for (int i = 1; i < 16; ++i) bamax = fmaxf(bamax, fabsf(f[i]));
+    const float t = __fmul_rn(__fmul_rn(g, bamax), 0.16666667163372039795f);
+    const uint32_t two = cvt_e4m3x2(__fmul_rn(t, 1.00000095367431640625f), __fmul_rn(t, 0.99999904632568359375f));
+    uint32_t b = two & 0xFFu;
+    if (__builtin_expect(b != (two >> 8), 0)) b = e4m3_scale_exact(bamax, g);
+    if (b == 0u) b = 0x80u;                       // a zero scale is stored as 0x80 (reference quirk)
+    BlockParams p;
+    p.sf = b;
+    p.g = g;
+    p.stored = (b & 0x7Fu) ? e4m3_value(b & 0x7Fu) : 0.0f;
+    const float invL = (b & 0x7Fu) ? __fmul_rn(g, rcp_approx(p.stored)) : 1.0f;
+    p.invL = invL;
+    const float2 ml = make_float2(invL * 0.99999904632568359375f, invL * 0.99999904632568359375f);
+    const float2 mh = make_float2(invL * 1.00000095367431640625f, invL * 1.00000095367431640625f);
     float lo[16], hi[16];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float2 f = make_float2(bf16lo(w[i]), bf16hi(w[i]));
-        const float2 q = __ffma2_rn(f, make_float2(p.invL, p.invL), make_float2(0.f, 0.f));
-        const float2 l = __fmul2_rn(q, make_float2(0.99999904632568359375f, 0.99999904632568359375f));
-        const float2 h = __fmul2_rn(q, make_float2(1.00000095367431640625f, 1.00000095367431640625f));
+        // + 0: turns -0.0 into +0.0 (the reference gives code 0 for -0.0); a negative product keeps its sign.
+        const float2 x2 = make_float2(f[2 * i], f[2 * i + 1]);
+        const float2 l = __ffma2_rn(x2, ml, make_float2(0.f, 0.f));
+        const float2 h = __ffma2_rn(x2, mh, make_float2(0.f, 0.f));
         lo[2 * i] = l.x; lo[2 * i + 1] = l.y;
         hi[2 * i] = h.x; hi[2 * i + 1] = h.y;
     }
@@ -251,7 +317,7 @@ __device__ __forceinline__ uint32_t quantize16_bf16(const uint32_t (&w)[8], floa
         c0 = resolve_codes(c0, l0 ^ c0, w[0], w[1], w[2], w[3], p);
         c1 = resolve_codes(c1, l1 ^ c1, w[4], w[5], w[6], w[7], p);
     }
-    return p.sf;
+    return b;
 }
 
 }  // namespace nvfp4b

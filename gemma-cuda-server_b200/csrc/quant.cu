@@ -3,9 +3,10 @@
 //
 // Replaces the reference's quant_kernel / nvfp4_quantize_activations (kernels/nvfp4_quant.cu:15-57), which is one
 // thread per 16-block with sixteen 4-byte loads and scattered single-byte scale stores.  Here:
-//   * work item = (row, 32 consecutive 16-element blocks): each lane loads its block with two 16-byte loads, so
-//     a warp reads 1 KB of contiguous bf16 and writes 256 contiguous code bytes; its 32 scale bytes land in 8
-//     runs of 4 consecutive bytes of the 128x4-tile layout.  Persistent warps prefetch the next item.
+//   * bf16 input: one warp per row, each lane quantising two blocks per step from two pairs of 16-byte loads (a
+//     warp reads 2 KB of contiguous row per step, writes 512 contiguous code bytes); fp32 input: work item = (row,
+//     32 consecutive blocks), persistent warps prefetching the next item.  Scale bytes land in runs of 4
+//     consecutive bytes of the 128x4-tile layout.
 //   * rounding is bit-exact against the reference's float64 numpy quantiser (see common.cuh); the per-element
 //     encode is straight-line with one exactness check per block.
 //   * padding rows (m >= M, up to the 128-row tile) and padding blocks (b >= K/16, up to the 4-block tile column)
@@ -18,19 +19,6 @@ namespace nvfp4b {
 
 template <typename T>
 struct InputTraits;
-
-template <>
-struct InputTraits<uint16_t> {   // bf16 bit patterns: 16 values = 2 x 16-byte loads
-    struct Raw { uint4 a, b; };
-    static __device__ __forceinline__ void load(const uint16_t* p, Raw& r) {
-        r.a = __ldg(reinterpret_cast<const uint4*>(p));
-        r.b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
-    }
-    static __device__ __forceinline__ uint32_t quantize(const Raw& r, float g, uint32_t& w0, uint32_t& w1) {
-        const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-        return quantize16_bf16(w, g, w0, w1);
-    }
-};
 
 template <>
 struct InputTraits<float> {      // fp32: 4 x 16-byte loads
@@ -49,7 +37,7 @@ struct InputTraits<float> {      // fp32: 4 x 16-byte loads
     }
 };
 
-// Work item = (row, 32 consecutive 16-element blocks): a warp's loads are 1 KB of contiguous bf16.  Rows are padded
+// fp32 input.  Work item = (row, 32 consecutive 16-element blocks): a warp's loads are 2 KB of contiguous fp32.  Rows are padded
 // to the 128-row tile and blocks to the 4-block tile column; padding lanes only write a zero scale byte.  Warps are
 // persistent (grid = 8 blocks per SM) and walk items with a stride, loading the next item while encoding the current
 // one, so every lane keeps 64 bytes in flight.  Scale bytes go to the tile layout (4 consecutive lanes -> 4
@@ -99,6 +87,61 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, 
         b = nb;
         ok = nok;
         raw = nraw;
+    }
+}
+
+// bf16 input, one warp per row (grid-stride over the rows padded to the 128-row tile): lane l takes blocks l and
+// l + 32 of each 64-block step, i.e. each step reads 2 KB of contiguous row as two 1 KB warp-wide runs, both loads
+// issued before either block is encoded.  Codes go out as 8-byte stores (a warp writes 256 contiguous bytes per
+// block set); scale bytes go to the tile layout (4 consecutive lanes -> 4 consecutive bytes).  Padding rows and
+// padding blocks only write zero scale bytes.  No integer division: rows advance by the warp count.
+__global__ void __launch_bounds__(256, 4) quantize_bf16_rows_kernel(const uint16_t* __restrict__ x, int M, int K,
+                                                                 float gscale, const float* __restrict__ d_amax,
+                                                                 uint8_t* __restrict__ packed,
+                                                                 uint8_t* __restrict__ scales, int tile_cols,
+                                                                 int rows_padded) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (int)((gridDim.x * blockDim.x) >> 5);
+    const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
+    const int kb = K >> 4, bmax = tile_cols * 4;
+    for (int m = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); m < rows_padded; m += warps) {
+        const bool real = m < M;
+        const uint16_t* xr = x + (size_t)(real ? m : 0) * K;
+        uint8_t* pr = packed + (size_t)(real ? m : 0) * (K >> 1);
+        uint8_t* sr = scales + (size_t)(m >> 7) * tile_cols * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4;
+        for (int b0 = 0; b0 < bmax; b0 += 64) {
+            const int ba = b0 + lane, bb = ba + 32;
+            const bool va = real && ba < kb, vb = real && bb < kb;
+            uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, c0 = a0, c1 = a0;
+            if (va) {
+                a0 = __ldg(reinterpret_cast<const uint4*>(xr + ba * 16));
+                a1 = __ldg(reinterpret_cast<const uint4*>(xr + ba * 16) + 1);
+            }
+            if (vb) {
+                c0 = __ldg(reinterpret_cast<const uint4*>(xr + bb * 16));
+                c1 = __ldg(reinterpret_cast<const uint4*>(xr + bb * 16) + 1);
+            }
+            if (ba < bmax) {
+                uint32_t sf = 0;
+                if (va) {
+                    const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    uint32_t q0, q1;
+                    sf = quantize16_bf16(w, g, q0, q1);
+                    *reinterpret_cast<uint2*>(pr + ba * 8) = make_uint2(q0, q1);
+                }
+                sr[(ba >> 2) * 512 + (ba & 3)] = (uint8_t)sf;
+            }
+            if (bb < bmax) {
+                uint32_t sf = 0;
+                if (vb) {
+                    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    uint32_t q0, q1;
+                    sf = quantize16_bf16(w, g, q0, q1);
+                    *reinterpret_cast<uint2*>(pr + bb * 8) = make_uint2(q0, q1);
+                }
+                sr[(bb >> 2) * 512 + (bb & 3)] = (uint8_t)sf;
+            }
+        }
     }
 }
 
@@ -172,9 +215,17 @@ static int launch_quantize(const T* x, int M, int K, float gscale, const float* 
     if (n_items > (1ll << 30)) return NVFP4B_ERR_SHAPE;
     long long blocks = (n_items + 7) / 8;
     const long long cap = (long long)sm_count() * 8;
-    if (blocks > cap) blocks = cap;
-    quantize_kernel<T><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed, scales,
-                                                                           tile_cols, chunks_per_row, (int)n_items);
+    if constexpr (sizeof(T) == 2) {
+        long long rb = (rows_padded + 7) / 8;                      // 8 warps (rows) per block
+        if (rb > cap) rb = cap;
+        quantize_bf16_rows_kernel<<<(unsigned)rb, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed,
+                                                                                  scales, tile_cols, rows_padded);
+    } else {
+        if (blocks > cap) blocks = cap;
+        quantize_kernel<T><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, M, K, gscale, d_amax, packed,
+                                                                               scales, tile_cols, chunks_per_row,
+                                                                               (int)n_items);
+    }
     return launch_status();
 }
 

@@ -60,7 +60,7 @@ def test_cfg1_sweep_dynamic_scale_bit_exact(T):
     _check_scales(sc, T, K, sf_ref)
 
 
-@pytest.mark.parametrize("M,K", [(1, 16), (3, 48), (129, 80), (200, 2048)])
+@pytest.mark.parametrize("M,K", [(1, 16), (3, 48), (129, 80), (200, 2048), (37, 4096), (9, 11264), (3, 24000)])
 def test_ragged_shapes(M, K):
     p = require_gpu()
     bits = orc.synth_bf16((M, K), 0.7, seed=M * 7 + K)
