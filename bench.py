@@ -40,9 +40,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "NVFP4 GEMM TFLOPS & quant GB/s vs roofline; MoE tokens/s at 1/2/4/8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram__bytes_read.sum + dram__bytes_write.sum of the dominant kernel per launch, from the ncu captures summarised
-# under profiles/ (None until a capture exists for the workload).
-NCU_TRAFFIC = {"quant": None, "gemm": None, "moe": None}
+# dram__bytes_read.sum + dram__bytes_write.sum (bytes) of the dominant kernel per launch, from the ncu captures
+# summarised under profiles/ (quantize_bf16_rows_kernel, nvf4_gemm_pair_kernel, the MoE gate/up GEMM).
+NCU_TRAFFIC = {"quant": 46.262272e6, "gemm": 335.105280e6, "moe": 366.175232e6}
 
 
 def parse_args():
@@ -521,7 +521,7 @@ def main():
         achieved = W.kernel_bytes / kern_s / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["quant"],
-                "kernel": "quantize_kernel<bf16>", "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
+                "kernel": "quantize_bf16_rows_kernel", "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
     elif W.name == "moe":
         achieved = W.kernel_flops / kern_s / 1e12
         fp4_peak = peaks["bf16_tflops"] * 4.0
