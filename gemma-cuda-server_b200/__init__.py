@@ -265,6 +265,15 @@ class MoeExperts:
             self.H, self.I, _ptr(self.w13[e]), _ptr(self.w13_scales[e]), _ptr(self.w2[e]), _ptr(self.w2_scales[e]),
             _stream(stream)))
 
+    def slice(self, e0: int, e1: int) -> "MoeExperts":
+        """Experts [e0, e1) as an arena of their own (views, no copy): the local shard of an expert-parallel rank."""
+        v = object.__new__(MoeExperts)
+        v.E, v.H, v.I = e1 - e0, self.H, self.I
+        v.w13_sf_bytes, v.w2_sf_bytes = self.w13_sf_bytes, self.w2_sf_bytes
+        for name in ("w13", "w13_scales", "w2", "w2_scales", "w1_gscale", "w3_gscale", "w2_gscale", "a2_gscale"):
+            setattr(v, name, getattr(self, name)[e0:e1])
+        return v
+
     def struct(self) -> _Experts:
         return _Experts(self.E, self.H, self.I, _ptr(self.w13), _ptr(self.w13_scales), _ptr(self.w2),
                         _ptr(self.w2_scales), _ptr(self.w1_gscale), _ptr(self.w3_gscale), _ptr(self.w2_gscale),
@@ -382,5 +391,60 @@ def moe_view(workspace, T: int, H: int, I: int, E: int, topk: int) -> dict:
         "a_scales": sl(v.a_scales, nvfp4_scale_buffer_bytes(rows, H), torch.uint8),
         "h_codes": sl(v.h_codes, rows * I // 2, torch.uint8).view(rows, I // 2),
         "h_scales": sl(v.h_scales, nvfp4_scale_buffer_bytes(rows, I), torch.uint8),
+        "y": sl(v.y, T * topk * H * 2, torch.float16).view(T * topk, H),
         "rows": rows,
     }
+
+
+# ---- expert parallelism (the collectives are torch.distributed's; see expert_parallel.py) ----------------------
+
+def _ep_sigs():
+    L = _moe_sigs()
+    if getattr(L, "_ep_ready", False):
+        return L
+    sig = {
+        "nvfp4b_ep_record_bytes": ([ctypes.c_int], ctypes.c_size_t),
+        "nvfp4b_ep_dispatch": ([_P, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                ctypes.c_float, _P, _P, _P, _P, _P], ctypes.c_int),
+        "nvfp4b_ep_expert_forward": ([_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_Experts), _P, _P],
+                                     ctypes.c_int),
+        "nvfp4b_ep_combine": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, _P],
+                              ctypes.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    L._ep_ready = True
+    return L
+
+
+def ep_record_bytes(H: int) -> int:
+    return int(_ep_sigs().nvfp4b_ep_record_bytes(H))
+
+
+def ep_dispatch(x, ids, weights, E: int, G: int, workspace, records, send_counts, in_gscale: float | None = None,
+                in_amax=None, stream=None) -> None:
+    """Source side: records [T*topk, ep_record_bytes(H)] uint8 sorted by destination rank; send_counts int32 [G]."""
+    T, H = x.shape
+    topk = ids.shape[1]
+    _check("ep_dispatch", _ep_sigs().nvfp4b_ep_dispatch(
+        _ptr(x), T, H, _ptr(ids), _ptr(weights), topk, E, G, float(in_gscale or 0.0), _ptr(in_amax),
+        _ptr(workspace), _ptr(records), _ptr(send_counts), _stream(stream)))
+
+
+def ep_expert_forward(records, n: int, n_cap: int, experts: MoeExperts, workspace, stream=None):
+    """Expert side: the weighted fp16 output rows of the n received records, as a view [n, H] of the workspace."""
+    ex = experts.struct()
+    _check("ep_expert_forward", _ep_sigs().nvfp4b_ep_expert_forward(
+        _ptr(records), n, n_cap, ctypes.byref(ex), _ptr(workspace), _stream(stream)))
+    return moe_view(workspace, n_cap, experts.H, experts.I, experts.E, 1)["y"][:n]
+
+
+def ep_combine(y_back, T: int, topk: int, E: int, workspace, out, accumulate: bool = False, stream=None):
+    """Source side: out[t] (+)= slot-ordered sum of the rows returned for token t."""
+    H = out.shape[1]
+    _check("ep_combine", _ep_sigs().nvfp4b_ep_combine(
+        _ptr(y_back), T, H, topk, E, _ptr(workspace), _ptr(out), MOE_ACCUMULATE if accumulate else 0,
+        _stream(stream)))
+    return out

@@ -59,6 +59,9 @@ struct Workspace {
     float* row_weight;
     int* row_assign;
     uint16_t* y;          // [T*topk, H] fp16 weighted expert outputs, assignment-major (deterministic combine)
+    float* row_gscale;    // [max_rows] per-row activation global scale (expert-parallel rows come from many ranks)
+    int* ep_ids;          // [T*topk] expert-parallel: local expert of each received record
+    float* ep_w;          // [T*topk] expert-parallel: router weight of each received record
     uint8_t* a_codes;
     uint8_t* a_scales;
     uint8_t* h_codes;
@@ -86,6 +89,9 @@ Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     w.row_weight = (float*)take((size_t)rows * 4);
     w.row_assign = (int*)take((size_t)rows * 4);
     w.y = (uint16_t*)take((size_t)n_assign * H * 2);
+    w.row_gscale = (float*)take((size_t)rows * 4);
+    w.ep_ids = (int*)take((size_t)n_assign * 4);
+    w.ep_w = (float*)take((size_t)n_assign * 4);
     w.a_codes = (uint8_t*)take((size_t)rows * (H / 2));
     w.a_scales = (uint8_t*)take(scale_bytes(rows, H));
     w.h_codes = (uint8_t*)take((size_t)rows * (I / 2));
@@ -297,7 +303,8 @@ __global__ void __launch_bounds__(256) moe_rank_kernel(const int* __restrict__ i
 __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ seg_start,
                                                       const int* __restrict__ seg_count, int kb, int tile_cols,
                                                       uint8_t* __restrict__ a_scales, int* __restrict__ row_token,
-                                                      float* __restrict__ row_weight, int* __restrict__ row_assign) {
+                                                      float* __restrict__ row_weight, int* __restrict__ row_assign,
+                                                      float* __restrict__ row_gscale) {
     const int e = blockIdx.x;
     const int start = seg_start[e], count = seg_count[e];
     const int pad0 = start + count, pad1 = start + (count + 127) / 128 * 128;
@@ -306,7 +313,12 @@ __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ se
         const int r = pad0 + i / tile_cols, tc = i % tile_cols;
         *reinterpret_cast<uint32_t*>(a_scales + ((long long)(r >> 7) * tile_cols + tc) * 512 + (r & 31) * 16 +
                                      ((r & 127) >> 5) * 4) = 0u;
-        if (tc == 0) { row_token[r] = -1; row_weight[r] = 0.f; row_assign[r] = -1; }
+        if (tc == 0) {
+            row_token[r] = -1;
+            row_weight[r] = 0.f;
+            row_assign[r] = -1;
+            if (row_gscale) row_gscale[r] = 1.f;     // any finite scale: padding rows hold zero codes
+        }
     }
     (void)kb;
 }
@@ -364,6 +376,7 @@ struct GateUpEpi {
     const float* a2_gscale;
     float in_gscale;
     const float* d_in_amax;
+    const float* row_gscale;   // if set: per-row activation global scale (overrides in_gscale / d_in_amax)
     float* h_amax;   // calibration output
     const int* row_token;
 
@@ -374,7 +387,7 @@ struct GateUpEpi {
                                             uint8_t*) const {
         const int e = ti.expert;
         const long long m = (long long)ti.a_row + row;
-        const float gin = d_in_amax ? gscale_from_amax(__ldg(d_in_amax)) : in_gscale;
+        const float gin = row_gscale ? __ldg(row_gscale + m) : d_in_amax ? gscale_from_amax(__ldg(d_in_amax)) : in_gscale;
         const float ag = __frcp_rn(gin * __ldg(w1_gscale + e));
         const float au = __frcp_rn(gin * __ldg(w3_gscale + e));
         const int jb0 = (ti.n0 + col_base) >> 5;          // first 16-wide block of h handled by this thread
@@ -534,6 +547,150 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const uint16_t* __rest
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// 6. expert parallelism: records exchanged between ranks (source: route + pack; expert: unpack + GEMMs; source:
+//    combine).  Record = [e2m1 codes H/2][logical e4m3 scales H/16][meta: local expert, router weight, activation
+//    global scale, 0], 16-byte aligned; a source packs its assignments sorted by expert, i.e. by destination rank
+//    (rank = expert / experts_per_rank), so each destination's records are one contiguous run.
+// ---------------------------------------------------------------------------------------------------------------
+
+struct EpMeta {
+    int expert;      // local expert on the destination rank
+    float weight;    // router weight of the assignment
+    float gscale;    // activation global scale the codes were made with
+    int pad;
+};
+
+__host__ __device__ inline size_t ep_record_bytes(int H) { return (size_t)(H / 2) + (size_t)(H / 16) + sizeof(EpMeta); }
+
+// Compact (unpadded) expert-sorted positions: chunk_base[c][e] = first row of expert e's assignments from chunk c;
+// send_counts[d] = records for destination rank d.
+__global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hist, int n_chunks, int E,
+                                                      int experts_per_rank, int G, int* __restrict__ chunk_base,
+                                                      int* __restrict__ seg_count, int* __restrict__ send_counts) {
+    __shared__ int start[257];
+    const int e = threadIdx.x;
+    int total = 0;
+    if (e < E)
+        for (int c = 0; c < n_chunks; ++c) total += hist[c * E + e];
+    start[e + 1] = e < E ? total : 0;
+    if (e == 0) start[0] = 0;
+    __syncthreads();
+    if (e == 0)
+        for (int i = 1; i <= E; ++i) start[i] += start[i - 1];
+    __syncthreads();
+    if (e < E) {
+        seg_count[e] = total;
+        int run = start[e];
+        for (int c = 0; c < n_chunks; ++c) {
+            chunk_base[c * E + e] = run;
+            run += hist[c * E + e];
+        }
+    }
+    if (e < G) send_counts[e] = start[min(E, (e + 1) * experts_per_rank)] - start[min(E, e * experts_per_rank)];
+}
+
+// Warp per token: quantise x[t] once (dynamic or static global scale), write one record per routed slot.
+__global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
+                                                      const int* __restrict__ dest, const int* __restrict__ ids,
+                                                      const float* __restrict__ weights, int experts_per_rank,
+                                                      float gscale, const float* __restrict__ d_amax,
+                                                      uint8_t* __restrict__ records) {
+    const int lane = threadIdx.x & 31;
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (t >= T) return;
+    const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
+    const size_t rb = ep_record_bytes(H);
+    const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
+    if (lane < topk && my_dest >= 0) {
+        EpMeta meta;
+        meta.expert = __ldg(ids + (long long)t * topk + lane) % experts_per_rank;
+        meta.weight = __ldg(weights + (long long)t * topk + lane);
+        meta.gscale = g;
+        meta.pad = 0;
+        *reinterpret_cast<EpMeta*>(records + (size_t)my_dest * rb + (H / 2) + (H / 16)) = meta;
+    }
+    const int kb = H >> 4;
+    const uint16_t* xr = x + (long long)t * H;
+    for (int b = lane; b - lane < kb; b += 32) {
+        uint32_t w0 = 0, w1 = 0, sf = 0;
+        if (b < kb) {
+            const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
+            const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
+            const uint32_t ww[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            sf = quantize16_bf16(ww, g, w0, w1);
+        }
+        for (int j = 0; j < topk; ++j) {
+            const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
+            if (r < 0 || b >= kb) continue;
+            uint8_t* rec = records + (size_t)r * rb;
+            *reinterpret_cast<uint2*>(rec + b * 8) = make_uint2(w0, w1);
+            rec[(H / 2) + b] = (uint8_t)sf;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* __restrict__ records, int n, int H,
+                                                      int* __restrict__ ids, float* __restrict__ w) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const EpMeta meta = *reinterpret_cast<const EpMeta*>(records + (size_t)i * ep_record_bytes(H) + (H / 2) + (H / 16));
+    ids[i] = meta.expert;
+    w[i] = meta.weight;
+}
+
+// Warp per received record: codes to its row of the padded expert-sorted operand, scales to the tile layout.
+__global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restrict__ records, int n, int H,
+                                                         const int* __restrict__ dest, uint8_t* __restrict__ a_codes,
+                                                         uint8_t* __restrict__ a_scales, float* __restrict__ row_gscale,
+                                                         int tile_cols) {
+    const int lane = threadIdx.x & 31;
+    const int i = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (i >= n) return;
+    const int r = __ldg(dest + i);
+    if (r < 0) return;
+    const uint8_t* rec = records + (size_t)i * ep_record_bytes(H);
+    const int kb = H >> 4;
+    for (int b = lane; b < kb; b += 32) {
+        *reinterpret_cast<uint2*>(a_codes + (long long)r * (H >> 1) + b * 8) =
+            *reinterpret_cast<const uint2*>(rec + b * 8);
+        a_scales[((long long)(r >> 7) * tile_cols + (b >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (b & 3)] =
+            rec[(H / 2) + b];
+    }
+    if (lane == 0) row_gscale[r] = reinterpret_cast<const EpMeta*>(rec + (H / 2) + (H / 16))->gscale;
+}
+
+// out[t] (+)= sum_j y_back[dest[t*k + j]] in slot order (fp32 accumulation of the fp16 rows sent back).
+__global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restrict__ y_back, int T, int H, int topk,
+                                                         const int* __restrict__ dest, float* __restrict__ out,
+                                                         int accumulate) {
+    const int lane = threadIdx.x & 31;
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (t >= T) return;
+    const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
+    float* dst = out + (long long)t * H;
+    for (int c = lane * 8; c < H; c += 256) {
+        float acc[8];
+        if (accumulate) {
+            const float4 u = *reinterpret_cast<const float4*>(dst + c), v = *reinterpret_cast<const float4*>(dst + c + 4);
+            acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        }
+        for (int j = 0; j < topk; ++j) {
+            const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
+            if (r < 0) continue;
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(y_back + (long long)r * H + c));
+            const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
+            acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+            acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+        }
+        *reinterpret_cast<float4*>(dst + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(dst + c + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
 using GroupCfg = KCfg<256, 4, 1, 8>;
 using DownCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // K = I is short: 3 stages + transpose tiles
 
@@ -564,7 +721,7 @@ int dispatch(const void* x, int T, const int* ids, const float* weights, int top
                                              w.row_weight, w.row_assign);
     const int tile_cols = (H / 16 + 3) / 4;
     moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
-                                     w.row_weight, w.row_assign);
+                                     w.row_weight, w.row_assign, nullptr);
     moe_quant_scatter_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
                                                          in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols);
     return launch_status();
@@ -572,7 +729,7 @@ int dispatch(const void* x, int T, const int* ids, const float* weights, int top
 
 template <bool CALIBRATE>
 int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, const float* d_in_amax, float* h_amax,
-            const Workspace& w, cudaStream_t s) {
+            const Workspace& w, cudaStream_t s, bool per_row_gscale = false) {
     const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
     const int rows = max_rows_for(T, E, topk);
     CUtensorMap ma, mb;
@@ -605,6 +762,7 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
     e.a2_gscale = ex->a2_gscale;
     e.in_gscale = in_gscale;
     e.d_in_amax = d_in_amax;
+    e.row_gscale = per_row_gscale ? w.row_gscale : nullptr;
     e.h_amax = h_amax;
     e.row_token = w.row_token;
     return launch_core<GroupCfg>(ma, mb, cp, sc, e, sm_count(), s);
@@ -639,7 +797,7 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
     if (deterministic) {
         DownEpi<true> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
         st = launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
-        if (st) return st;
+        if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
         moe_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(w.y, T, H, topk, out, accumulate ? 1 : 0);
         return launch_status();
     }
@@ -649,6 +807,45 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
     }
     DownEpi<false> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
     return launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
+}
+
+
+// expert parallelism, source side: plan + pack the records of this rank's assignments.
+int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E, int G,
+                float in_gscale, const float* d_in_amax, const Workspace& w, uint8_t* records, int* send_counts,
+                cudaStream_t s) {
+    const int n_assign = T * topk;
+    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
+    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
+    ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, w.chunk_base, w.seg_count, send_counts);
+    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
+                                             w.row_weight, w.row_assign);
+    ep_pack_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest, ids, weights,
+                                               E / G, in_gscale, d_in_amax, records);
+    return launch_status();
+}
+
+// expert parallelism, expert side: received records -> padded expert-sorted operand -> gate/up -> down GEMM, leaving
+// each record's weighted output row (fp16) in w.y in record order.
+int ep_expert(const uint8_t* records, int n, const nvfp4b_moe_experts* ex, const Workspace& w, cudaStream_t s) {
+    const int H = ex->hidden, E = ex->num_experts;
+    const int n_chunks = (n + kChunk - 1) / kChunk;
+    ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, w.ep_ids, w.ep_w);
+    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist);
+    moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
+                                      w.tile_expert);
+    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, w.ep_w, n, E, 1, w.chunk_base, w.dest, w.row_token,
+                                             w.row_weight, w.row_assign);
+    const int tile_cols = (H / 16 + 3) / 4;
+    moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
+                                     w.row_weight, w.row_assign, w.row_gscale);
+    ep_scatter_kernel<<<(n + 7) / 8, 256, 0, s>>>(records, n, H, w.dest, w.a_codes, w.a_scales, w.row_gscale,
+                                                  tile_cols);
+    int st = launch_status();
+    if (st) return st;
+    st = gate_up<false>(ex, n, 1, 1.0f, nullptr, nullptr, w, s, true);
+    if (st) return st;
+    return down(ex, n, 1, w.ep_w, nullptr, 0, w, s);
 }
 
 // Gate/up interleave: w13 row 32g + r <- gate row 16g + r; 32g + 16 + r <- up row 16g + r.
@@ -923,5 +1120,46 @@ extern "C" int nvfp4b_moe_pack_expert(const uint8_t* gate, const uint8_t* gate_s
     if (e != cudaSuccess) return record_cuda_error(e);
     const int st = nvfp4b_swizzle_scales(down_scales, w2_scales_dst, H, I, stream);
     if (st) return st;
+    return launch_status();
+}
+
+// ---- expert parallelism ------------------------------------------------------------------------------------------
+
+extern "C" size_t nvfp4b_ep_record_bytes(int H) { return H > 0 && H % 256 == 0 ? ep_record_bytes(H) : 0; }
+
+extern "C" int nvfp4b_ep_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E,
+                                  int G, float in_gscale, const float* d_in_amax, void* workspace, uint8_t* records,
+                                  int* send_counts, void* stream) {
+    if (!x || !ids || !weights || !workspace || !records || !send_counts) return NVFP4B_ERR_NULL;
+    if (T <= 0 || H <= 0 || (H % 256) || topk <= 0 || topk > 16 || E <= 0 || E > 256 || G <= 0 || G > 256 ||
+        (E % G) || topk > E)
+        return NVFP4B_ERR_SHAPE;
+    if (!aligned16(x) || !aligned16(records) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    const Workspace w = carve(workspace, T, H, 32, E, topk);
+    return ep_dispatch(x, T, H, ids, weights, topk, E, G, in_gscale, d_in_amax, w, records, send_counts,
+                       (cudaStream_t)stream);
+}
+
+extern "C" int nvfp4b_ep_expert_forward(const uint8_t* records, int n, int n_cap, const nvfp4b_moe_experts* ex,
+                                        void* workspace, void* stream) {
+    if (!records || !workspace) return NVFP4B_ERR_NULL;
+    const int st = check_experts(ex);
+    if (st) return st;
+    if (n < 0 || n > n_cap || n_cap <= 0) return NVFP4B_ERR_SHAPE;
+    if (!aligned16(records) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    if (n == 0) return NVFP4B_OK;
+    const Workspace w = carve(workspace, n_cap, ex->hidden, ex->inter, ex->num_experts, 1);
+    return ep_expert(records, n, ex, w, (cudaStream_t)stream);
+}
+
+extern "C" int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk, int E, const void* workspace,
+                                 float* out, int flags, void* stream) {
+    if (!y_back || !workspace || !out) return NVFP4B_ERR_NULL;
+    if (T <= 0 || H <= 0 || (H % 256) || topk <= 0 || topk > 16 || E <= 0) return NVFP4B_ERR_SHAPE;
+    if (flags & ~NVFP4B_MOE_ACCUMULATE) return NVFP4B_ERR_ARG;
+    if (!aligned16(y_back) || !aligned16(out)) return NVFP4B_ERR_ALIGN;
+    const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
+    ep_combine_kernel<<<(T + 7) / 8, 256, 0, (cudaStream_t)stream>>>(y_back, T, H, topk, w.dest, out,
+                                                                    (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0);
     return launch_status();
 }
