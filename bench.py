@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", choices=["quant", "gemm", "moe"], default="quant")
+    ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep"], default="quant")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
@@ -373,6 +373,112 @@ class MoeWorkload:
         return S / el, f"{S} tokens of cfg3 through the W4A4 experts() path (dequantised experts, float32)"
 
 
+class EpWorkload:
+    """cfg4: expert-parallel decode/verify stack on G GPUs -- 30 stacked MoE FFN layers shaped as cfg3 (H=2816,
+    128 experts of I=704, top-8), 512 rows (32 sequences x 16 draft tokens) per rank per step, experts sharded
+    128/G per GPU, NCCL all-to-all of the routed records and of the returned rows per layer.  Layers are chained
+    through an fp32 residual stream (each layer adds its MoE output, the next layer reads it back as bf16)."""
+    name = "ep"
+    unit = "tokens/s"
+    dtype = "nvfp4"
+
+    def __init__(self, pkg, torch, orc, rank=0, world=1, group=None, T=512, H=2816, I=704, E=128, topk=8, L=30):
+        import numpy as np
+        import gemma_cuda_server_b200.expert_parallel as epm
+        self.pkg, self.torch = pkg, torch
+        self.T, self.H, self.I, self.E, self.topk, self.L, self.G = T, H, I, E, topk, L, world
+        El = E // world
+        gen = torch.Generator(device="cuda").manual_seed(4000 + rank)
+        self.x0 = torch.randn((T, H), generator=gen, device="cuda").to(torch.bfloat16)
+        self.x = torch.empty_like(self.x0)
+        self.res = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        cal_ws = pkg.moe_workspace(T, H, I, El, topk)
+        self.layers = []
+        x = self.x0.clone()
+        res = x.float()
+        for l in range(L):
+            lg = torch.Generator(device="cuda").manual_seed(5000 + l)              # router: same on every rank
+            proj = (torch.randn((E, H), generator=lg, device="cuda") * 0.02).to(torch.bfloat16)
+            wg = torch.Generator(device="cuda").manual_seed(6000 + 131 * l + rank)  # this rank's expert shard
+            arena = pkg.MoeExperts(El, H, I)
+            w13 = (torch.randn((El * 2 * I, H), generator=wg, device="cuda") * 0.02).to(torch.bfloat16)
+            g = float(orc.global_scale_from_amax(pkg.amax(w13).item()))
+            pkg.quantize(w13, gscale=g, packed=arena.w13.view(El * 2 * I, H // 2), scales=arena.w13_scales.view(-1))
+            del w13
+            arena.w1_gscale.fill_(g)
+            arena.w3_gscale.fill_(g)
+            w2 = (torch.randn((El * H, I), generator=wg, device="cuda") * 0.02).to(torch.bfloat16)
+            g2 = float(orc.global_scale_from_amax(pkg.amax(w2).item()))
+            pkg.quantize(w2, gscale=g2, packed=arena.w2.view(El * H, I // 2), scales=arena.w2_scales.view(-1))
+            del w2
+            arena.w2_gscale.fill_(g2)
+            ops = epm.KernelOps(pkg, arena, E, topk, T_cap=T, G=world)
+            Ld = dict(proj=proj, arena=arena, ops=ops, layer=epm.ExpertParallelMoE(ops, group),
+                      amax=torch.zeros(1, device="cuda"), ids=torch.empty((T, topk), dtype=torch.int32, device="cuda"),
+                      w=torch.empty((T, topk), dtype=torch.float32, device="cuda"))
+            # static down-projection input scales: calibrate this rank's experts on this layer's real input, with
+            # every token sent to topk random local experts (each expert sees ~T*topk/El rows)
+            pkg.amax(x, out=Ld["amax"])
+            cal_ids = torch.argsort(torch.rand((T, El), generator=wg, device="cuda"), dim=1)[:, :topk].int().contiguous()
+            cal_w = torch.full((T, topk), 1.0 / topk, device="cuda")
+            h_amax = pkg.moe_calibrate(x, cal_ids, cal_w, arena, cal_ws, in_amax=Ld["amax"])
+            arena.a2_gscale.copy_(torch.from_numpy(np.array(
+                [orc.global_scale_from_amax(v) for v in h_amax.cpu().numpy()], np.float32)))
+            pkg.moe_route(x, proj, topk, ops.src_ws, ids=Ld["ids"], weights=Ld["w"])
+            Ld["layer"].forward(x, Ld["ids"], Ld["w"], res, in_amax=Ld["amax"], accumulate=True)
+            x.copy_(res)
+            self.layers.append(Ld)
+        torch.cuda.synchronize()
+        del cal_ws
+        self.units_per_step = T                                   # rows of this rank; value() scales by G
+        self.launches_per_step = 16 * L   # per layer: amax, router x2, dispatch x4, expert x8, combine
+        self.kernel_flops = 2.0 * T * topk * 3 * I * H            # expert GEMMs of one layer at even routing
+        self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
+        self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_per_gpu": T, "hidden": H,
+                       "experts": E, "experts_per_gpu": El, "inter": I, "topk": topk,
+                       "exchange": "NCCL all-to-all of NVFP4 records and fp16 rows per layer",
+                       "l2": "flushed between steps (256 MiB write + 256 MiB read)", "step_flops": self.step_flops}
+
+    def step(self, mark=None):
+        p, k = self.pkg, self.topk
+        self.x.copy_(self.x0)
+        self.res.copy_(self.x0)
+        for li, Ld in enumerate(self.layers):
+            p.amax(self.x, out=Ld["amax"])
+            p.moe_route(self.x, Ld["proj"], k, Ld["ops"].src_ws, ids=Ld["ids"], weights=Ld["w"])
+            Ld["layer"].forward(self.x, Ld["ids"], Ld["w"], self.res, in_amax=Ld["amax"], accumulate=True,
+                                mark=mark if li == 0 else None)
+            self.x.copy_(self.res)
+
+    def value(self, seconds_per_step):
+        return self.units_per_step / seconds_per_step
+
+    def e2e_setup(self):
+        t = self.torch
+        self.h_x = t.empty((self.T, self.H), dtype=t.bfloat16, pin_memory=True)
+        self.h_x.copy_(self.x0.cpu())
+        self.h_out = t.empty((self.T, self.H), dtype=t.float32, pin_memory=True)
+        return self.T * self.H * 2, self.T * self.H * 4
+
+    def e2e_step(self):
+        self.x0.copy_(self.h_x, non_blocking=True)
+        if getattr(self, "graph", None) is not None:
+            self.graph.replay()
+        else:
+            self.step()
+        self.h_out.copy_(self.res, non_blocking=True)
+
+    def cpu_run(self, native, orc, seconds):
+        """Layer 0 of the stack through the reference's experts() semantics (W4A4, dequantised experts, float32)
+        on a token sample; tokens/s for the 30-layer stack = layer rate / 30."""
+        Ld = self.layers[0]
+        m = MoeWorkload.__new__(MoeWorkload)
+        m.ids, m.wts, m.x, m.in_amax, m.arena = Ld["ids"], Ld["w"], self.x0, Ld["amax"], Ld["arena"]
+        m.H, m.I, m.topk = self.H, self.I, self.topk
+        rate, sample = MoeWorkload.cpu_run(m, native, orc, seconds)
+        return rate / self.L, sample.replace("cfg3", "layer 0 of cfg4") + f"; stack rate = layer rate / {self.L}"
+
+
 # ----------------------------------------------------------------------------------------------------------------
 
 def cpu_cores():
@@ -437,7 +543,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     pkg = load_package()
     pkg.lib()
-    W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload}[args.workload](pkg, torch, orc)
+    if args.workload == "ep":
+        W = EpWorkload(pkg, torch, orc, rank=rank, world=world)
+    else:
+        W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload}[args.workload](pkg, torch, orc)
     # L2 flush between steps: write a 256 MiB buffer (evicts the step's data), then read another 256 MiB buffer so
     # the L2 is left holding clean lines (otherwise the next step would pay the flush's own write-backs).
     flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -465,6 +574,15 @@ def main():
             flush.zero_()
             W.step()
         barrier()
+        # The expert-parallel stack (30 layers of ~16 small launches and 3 collectives) is launch-bound at 512 rows:
+        # capture one step in a CUDA graph (fixed-size buffers, no host reads inside) and replay it.
+        graph = None
+        if W.name == "ep":
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                W.step()
+            barrier()
+            W.graph = graph
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         marks = [{} for _ in range(args.steps)]
@@ -476,18 +594,39 @@ def main():
                 ev = torch.cuda.Event(enable_timing=True)
                 ev.record(stream)
                 marks[i][name] = ev
-            W.step(mark)
+            if graph is not None:
+                graph.replay()
+            else:
+                W.step(mark)
             stops[i].record(stream)
         barrier()
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
-        kern_ms = [m["kernel"].elapsed_time(m["kernel_end"]) for m in marks]
-        # sustained window for the clock record (same steps, untimed)
-        t_end = time.perf_counter() + args.clock_seconds
-        while time.perf_counter() < t_end:
-            for _ in range(20):
+        if graph is not None:          # kernel marks from eager steps (events cannot be taken inside the replay)
+            marks = [{} for _ in range(3)]
+            for i in range(3):
                 flush.zero_()
+
+                def mark(name, i=i):
+                    ev = torch.cuda.Event(enable_timing=True)
+                    ev.record(stream)
+                    marks[i][name] = ev
+                W.step(mark)
+            barrier()
+        kern_ms = [m["kernel"].elapsed_time(m["kernel_end"]) for m in marks]
+        # sustained window for the clock record (same steps, untimed); a step count all ranks agree on
+        per_step = torch.tensor([sum(step_ms) / len(step_ms)], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(per_step, op=dist.ReduceOp.MAX)
+        n_clock = max(1, min(2000, int(args.clock_seconds * 1e3 / max(float(per_step.item()), 1e-3))))
+        for i in range(n_clock):
+            flush.zero_()
+            if graph is not None:
+                graph.replay()
+            else:
                 W.step()
-            torch.cuda.synchronize()
+            if i % 20 == 19:
+                torch.cuda.synchronize()
+        barrier()
     clocks = sampler.summary()
 
     total_ms = sum(step_ms)
@@ -530,6 +669,15 @@ def main():
                 "kernel": "nvf4_gemm_kernel<GroupedSched, GateUpEpi> (grouped gate/up, GELU + NVFP4 requant)",
                 "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
                 "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
+    elif W.name == "ep":
+        n_recv = int(W.layers[0]["ops"].counts[W.G:].sum().item())   # records this rank's experts ran in layer 0
+        achieved = 2.0 * n_recv * 3 * W.I * W.H / kern_s / 1e12
+        fp4_peak = peaks["bf16_tflops"] * 4.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
+                "frac": achieved / fp4_peak, "traffic": None,
+                "kernel": "expert side of one layer (record scatter, grouped gate/up and down GEMMs)",
+                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
+                "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
     else:
         achieved = W.units_per_step / kern_s / 1e12
         fp4_peak = peaks["bf16_tflops"] * 4.0
@@ -545,6 +693,9 @@ def main():
         cpu = {"value": cv, "unit": W.unit, "cores": native.num_threads() if W.name == "quant" else cpu_cores(),
                "kind": "port", "sample": sample}
 
+    if W.name == "ep":
+        W.config["capacity_overflow"] = bool(sum(int(Ld["ops"].overflow.item()) for Ld in W.layers))
+        W.config["graph"] = "one CUDA graph per step" if getattr(W, "graph", None) is not None else "eager"
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -552,10 +703,14 @@ def main():
             "metric": METRIC, "value": value, "unit": W.unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded, shapes of BASELINE.json configs)",
-            "config": {**W.config, "parallelism": f"replicas x{world}"},
+            "config": {**W.config, "parallelism": f"expert parallel x{world}" if W.name == "ep" else f"replicas x{world}"},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": W.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": W.launches_per_step * args.steps, "clocks": clocks}))
+    if getattr(W, "graph", None) is not None:      # a graph holding NCCL calls must go before the process group
+        W.graph = None
+        graph = None
+        torch.cuda.synchronize()
     if world > 1:
         dist.destroy_process_group()
 

@@ -405,8 +405,8 @@ def _ep_sigs():
     sig = {
         "nvfp4b_ep_record_bytes": ([ctypes.c_int], ctypes.c_size_t),
         "nvfp4b_ep_dispatch": ([_P, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                ctypes.c_float, _P, _P, _P, _P, _P], ctypes.c_int),
-        "nvfp4b_ep_expert_forward": ([_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_Experts), _P, _P],
+                                ctypes.c_int, ctypes.c_float, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+        "nvfp4b_ep_expert_forward": ([_P, ctypes.c_int, ctypes.c_int, _P, ctypes.POINTER(_Experts), _P, _P],
                                      ctypes.c_int),
         "nvfp4b_ep_combine": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, _P],
                               ctypes.c_int),
@@ -423,22 +423,24 @@ def ep_record_bytes(H: int) -> int:
     return int(_ep_sigs().nvfp4b_ep_record_bytes(H))
 
 
-def ep_dispatch(x, ids, weights, E: int, G: int, workspace, records, send_counts, in_gscale: float | None = None,
-                in_amax=None, stream=None) -> None:
-    """Source side: records [T*topk, ep_record_bytes(H)] uint8 sorted by destination rank; send_counts int32 [G]."""
+def ep_dispatch(x, ids, weights, E: int, G: int, capacity: int, workspace, records, send_counts, overflow,
+                in_gscale: float | None = None, in_amax=None, stream=None) -> None:
+    """Source side: records [G * capacity, ep_record_bytes(H)] uint8, destination-major slots; send_counts int32
+    [G]; overflow int32 [1] (or-ed with 1 when a destination gets more than capacity records)."""
     T, H = x.shape
     topk = ids.shape[1]
     _check("ep_dispatch", _ep_sigs().nvfp4b_ep_dispatch(
-        _ptr(x), T, H, _ptr(ids), _ptr(weights), topk, E, G, float(in_gscale or 0.0), _ptr(in_amax),
-        _ptr(workspace), _ptr(records), _ptr(send_counts), _stream(stream)))
+        _ptr(x), T, H, _ptr(ids), _ptr(weights), topk, E, G, capacity, float(in_gscale or 0.0), _ptr(in_amax),
+        _ptr(workspace), _ptr(records), _ptr(send_counts), _ptr(overflow), _stream(stream)))
 
 
-def ep_expert_forward(records, n: int, n_cap: int, experts: MoeExperts, workspace, stream=None):
-    """Expert side: the weighted fp16 output rows of the n received records, as a view [n, H] of the workspace."""
+def ep_expert_forward(records, G: int, capacity: int, recv_counts, experts: MoeExperts, workspace, stream=None):
+    """Expert side: the weighted fp16 output rows of the G * capacity received slots, a view [G * capacity, H] of
+    the workspace (rows of empty slots are undefined)."""
     ex = experts.struct()
     _check("ep_expert_forward", _ep_sigs().nvfp4b_ep_expert_forward(
-        _ptr(records), n, n_cap, ctypes.byref(ex), _ptr(workspace), _stream(stream)))
-    return moe_view(workspace, n_cap, experts.H, experts.I, experts.E, 1)["y"][:n]
+        _ptr(records), G, capacity, _ptr(recv_counts), ctypes.byref(ex), _ptr(workspace), _stream(stream)))
+    return moe_view(workspace, G * capacity, experts.H, experts.I, experts.E, 1)["y"]
 
 
 def ep_combine(y_back, T: int, topk: int, E: int, workspace, out, accumulate: bool = False, stream=None):

@@ -564,10 +564,13 @@ struct EpMeta {
 __host__ __device__ inline size_t ep_record_bytes(int H) { return (size_t)(H / 2) + (size_t)(H / 16) + sizeof(EpMeta); }
 
 // Compact (unpadded) expert-sorted positions: chunk_base[c][e] = first row of expert e's assignments from chunk c;
-// send_counts[d] = records for destination rank d.
+// dst_start[d] = first position of destination rank d's run; send_counts[d] = records for rank d, at most
+// `capacity` (the fixed slot count per destination); more sets *overflow (the excess is not sent).
 __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hist, int n_chunks, int E,
-                                                      int experts_per_rank, int G, int* __restrict__ chunk_base,
-                                                      int* __restrict__ seg_count, int* __restrict__ send_counts) {
+                                                      int experts_per_rank, int G, int capacity,
+                                                      int* __restrict__ chunk_base, int* __restrict__ seg_count,
+                                                      int* __restrict__ dst_start, int* __restrict__ send_counts,
+                                                      int* __restrict__ overflow) {
     __shared__ int start[257];
     const int e = threadIdx.x;
     int total = 0;
@@ -587,13 +590,21 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hi
             run += hist[c * E + e];
         }
     }
-    if (e < G) send_counts[e] = start[min(E, (e + 1) * experts_per_rank)] - start[min(E, e * experts_per_rank)];
+    if (e < G) {
+        const int n = start[min(E, (e + 1) * experts_per_rank)] - start[min(E, e * experts_per_rank)];
+        dst_start[e] = start[min(E, e * experts_per_rank)];
+        send_counts[e] = min(n, capacity);
+        if (n > capacity) atomicOr(overflow, 1);
+    }
 }
 
 // Warp per token: quantise x[t] once (dynamic or static global scale), write one record per routed slot.
+// dest[a] on entry: compact position; on exit: the record slot d * capacity + (position - dst_start[d]), or -1
+// when that is past the capacity (overflowed, not sent).
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
-                                                      const int* __restrict__ dest, const int* __restrict__ ids,
+                                                      int* __restrict__ dest, const int* __restrict__ ids,
                                                       const float* __restrict__ weights, int experts_per_rank,
+                                                      int capacity, const int* __restrict__ dst_start,
                                                       float gscale, const float* __restrict__ d_amax,
                                                       uint8_t* __restrict__ records) {
     const int lane = threadIdx.x & 31;
@@ -601,7 +612,17 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
     if (t >= T) return;
     const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
     const size_t rb = ep_record_bytes(H);
-    const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
+    int my_dest = -1;
+    if (lane < topk) {
+        const long long a = (long long)t * topk + lane;
+        const int pos = dest[a];
+        if (pos >= 0) {
+            const int d = __ldg(ids + a) / experts_per_rank;
+            const int i = pos - __ldg(dst_start + d);
+            my_dest = i < capacity ? d * capacity + i : -1;
+        }
+        dest[a] = my_dest;
+    }
     if (lane < topk && my_dest >= 0) {
         EpMeta meta;
         meta.expert = __ldg(ids + (long long)t * topk + lane) % experts_per_rank;
@@ -630,10 +651,17 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
     }
 }
 
-__global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* __restrict__ records, int n, int H,
-                                                      int* __restrict__ ids, float* __restrict__ w) {
+// Slot i = s * capacity + j holds a record iff j < recv_counts[s]; empty slots get expert -1 (skipped by the plan).
+__global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* __restrict__ records, int n, int H, int capacity,
+                                                      const int* __restrict__ recv_counts, int* __restrict__ ids,
+                                                      float* __restrict__ w) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
+    if (i % capacity >= __ldg(recv_counts + i / capacity)) {
+        ids[i] = -1;
+        w[i] = 0.f;
+        return;
+    }
     const EpMeta meta = *reinterpret_cast<const EpMeta*>(records + (size_t)i * ep_record_bytes(H) + (H / 2) + (H / 16));
     ids[i] = meta.expert;
     w[i] = meta.weight;
@@ -812,25 +840,28 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
 
 // expert parallelism, source side: plan + pack the records of this rank's assignments.
 int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E, int G,
-                float in_gscale, const float* d_in_amax, const Workspace& w, uint8_t* records, int* send_counts,
-                cudaStream_t s) {
+                int capacity, float in_gscale, const float* d_in_amax, const Workspace& w, uint8_t* records,
+                int* send_counts, int* overflow, cudaStream_t s) {
     const int n_assign = T * topk;
     const int n_chunks = (n_assign + kChunk - 1) / kChunk;
     moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
-    ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, w.chunk_base, w.seg_count, send_counts);
+    ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, capacity, w.chunk_base, w.seg_count,
+                                     w.seg_start, send_counts, overflow);
     moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
                                              w.row_weight, w.row_assign);
     ep_pack_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest, ids, weights,
-                                               E / G, in_gscale, d_in_amax, records);
+                                               E / G, capacity, w.seg_start, in_gscale, d_in_amax, records);
     return launch_status();
 }
 
 // expert parallelism, expert side: received records -> padded expert-sorted operand -> gate/up -> down GEMM, leaving
 // each record's weighted output row (fp16) in w.y in record order.
-int ep_expert(const uint8_t* records, int n, const nvfp4b_moe_experts* ex, const Workspace& w, cudaStream_t s) {
+int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_counts, const nvfp4b_moe_experts* ex,
+              const Workspace& w, cudaStream_t s) {
     const int H = ex->hidden, E = ex->num_experts;
+    const int n = G * capacity;
     const int n_chunks = (n + kChunk - 1) / kChunk;
-    ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, w.ep_ids, w.ep_w);
+    ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, capacity, recv_counts, w.ep_ids, w.ep_w);
     moe_hist_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist);
     moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
                                       w.tile_expert);
@@ -1128,28 +1159,27 @@ extern "C" int nvfp4b_moe_pack_expert(const uint8_t* gate, const uint8_t* gate_s
 extern "C" size_t nvfp4b_ep_record_bytes(int H) { return H > 0 && H % 256 == 0 ? ep_record_bytes(H) : 0; }
 
 extern "C" int nvfp4b_ep_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E,
-                                  int G, float in_gscale, const float* d_in_amax, void* workspace, uint8_t* records,
-                                  int* send_counts, void* stream) {
-    if (!x || !ids || !weights || !workspace || !records || !send_counts) return NVFP4B_ERR_NULL;
+                                  int G, int capacity, float in_gscale, const float* d_in_amax, void* workspace,
+                                  uint8_t* records, int* send_counts, int* overflow, void* stream) {
+    if (!x || !ids || !weights || !workspace || !records || !send_counts || !overflow) return NVFP4B_ERR_NULL;
     if (T <= 0 || H <= 0 || (H % 256) || topk <= 0 || topk > 16 || E <= 0 || E > 256 || G <= 0 || G > 256 ||
-        (E % G) || topk > E)
+        (E % G) || topk > E || capacity <= 0)
         return NVFP4B_ERR_SHAPE;
     if (!aligned16(x) || !aligned16(records) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
     const Workspace w = carve(workspace, T, H, 32, E, topk);
-    return ep_dispatch(x, T, H, ids, weights, topk, E, G, in_gscale, d_in_amax, w, records, send_counts,
-                       (cudaStream_t)stream);
+    return ep_dispatch(x, T, H, ids, weights, topk, E, G, capacity, in_gscale, d_in_amax, w, records, send_counts,
+                       overflow, (cudaStream_t)stream);
 }
 
-extern "C" int nvfp4b_ep_expert_forward(const uint8_t* records, int n, int n_cap, const nvfp4b_moe_experts* ex,
-                                        void* workspace, void* stream) {
-    if (!records || !workspace) return NVFP4B_ERR_NULL;
+extern "C" int nvfp4b_ep_expert_forward(const uint8_t* records, int G, int capacity, const int* recv_counts,
+                                        const nvfp4b_moe_experts* ex, void* workspace, void* stream) {
+    if (!records || !recv_counts || !workspace) return NVFP4B_ERR_NULL;
     const int st = check_experts(ex);
     if (st) return st;
-    if (n < 0 || n > n_cap || n_cap <= 0) return NVFP4B_ERR_SHAPE;
+    if (G <= 0 || capacity <= 0 || (long long)G * capacity > (1 << 26)) return NVFP4B_ERR_SHAPE;
     if (!aligned16(records) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
-    if (n == 0) return NVFP4B_OK;
-    const Workspace w = carve(workspace, n_cap, ex->hidden, ex->inter, ex->num_experts, 1);
-    return ep_expert(records, n, ex, w, (cudaStream_t)stream);
+    const Workspace w = carve(workspace, G * capacity, ex->hidden, ex->inter, ex->num_experts, 1);
+    return ep_expert(records, G, capacity, recv_counts, ex, w, (cudaStream_t)stream);
 }
 
 extern "C" int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk, int E, const void* workspace,

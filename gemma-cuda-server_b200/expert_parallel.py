@@ -6,15 +6,17 @@ sum).  This is the expert-parallel form of the same computation.  One layer, per
 
   1. route (caller): ids [T, k], weights [T, k]
   2. ops.dispatch: one record per assignment (NVFP4 codes + scales of the token, local expert, router weight,
-     activation global scale), sorted by destination rank; per-rank counts
-  3. all-to-all of the counts, then ONE device->host read of the count vectors (they are the split sizes)
-  4. all-to-all of the records (uneven splits)
-  5. ops.expert: the local experts on the received records -> weighted fp16 rows [n_recv, H]
-  6. all-to-all of the rows back to their sources (the reverse splits)
-  7. ops.combine: slot-ordered fp32 sum into out (bit-identical to the single-GPU layer at G = 1)
+     activation global scale) into fixed destination-major slots (capacity per destination); counts per rank
+  3. all-to-all of the counts (G ints) and of the record slots
+  4. ops.expert: the local experts on the received slots -> weighted fp16 rows, one per slot
+  5. all-to-all of the row slots back to their sources
+  6. ops.combine: slot-ordered fp32 sum into out (bit-identical to the single-GPU layer at G = 1)
 
-`ops` does the device work; KernelOps is the sm_100a implementation (the C ABI of libnvfp4_b200.so).  Steps 3, 4
-and 6 are the only collectives, issued on the caller's current stream, in the same order on every rank.
+Every buffer has a fixed size, so nothing is read back to the host and a whole stack of layers can be captured in
+one CUDA graph.  A destination receiving more than `capacity` records from one source sets the overflow flag
+(check with overflowed() after the step); capacity = T_cap * topk never overflows.  `ops` does the device work;
+KernelOps is the sm_100a implementation (the C ABI of libnvfp4_b200.so).  The collectives are issued on the
+caller's current stream, in the same order on every rank.
 """
 from __future__ import annotations
 
@@ -23,9 +25,13 @@ import torch.distributed as dist
 
 
 class KernelOps:
-    """Device side of one expert-parallel layer on this rank: buffers sized for up to T_cap tokens per rank."""
+    """Device side of one expert-parallel layer on this rank: buffers sized for up to T_cap tokens per rank and
+    `capacity` records per (source, destination) pair.  The all-to-alls move every slot, so the default is the even
+    share n = T_cap * topk / G plus 8 sqrt(n) + 32 (eight standard deviations of a uniform router's count), at most
+    T_cap * topk (which cannot overflow)."""
 
-    def __init__(self, pkg, experts, E: int, topk: int, T_cap: int, G: int, device="cuda"):
+    def __init__(self, pkg, experts, E: int, topk: int, T_cap: int, G: int, capacity: int | None = None,
+                 device="cuda"):
         if E % G:
             raise ValueError(f"{E} experts do not split over {G} ranks")
         if experts.E != E // G:
@@ -33,26 +39,31 @@ class KernelOps:
         self.pkg, self.experts, self.E, self.topk, self.T_cap, self.G = pkg, experts, E, topk, T_cap, G
         H, I = experts.H, experts.I
         self.H = H
+        if capacity is None:
+            share = T_cap * topk / G
+            capacity = min(T_cap * topk, int(share + 8 * share ** 0.5 + 32 + 15) // 16 * 16)
+        self.capacity = capacity
         self.record_bytes = pkg.ep_record_bytes(H)
-        self.n_cap = G * T_cap * topk                       # worst case: every rank routes everything here
+        n = G * capacity
         self.src_ws = pkg.moe_workspace(T_cap, H, 32, E, topk, device=device)
-        self.exp_ws = pkg.moe_workspace(self.n_cap, H, I, E // G, 1, device=device)
-        self.send = torch.empty((T_cap * topk, self.record_bytes), dtype=torch.uint8, device=device)
-        self.recv = torch.empty((self.n_cap, self.record_bytes), dtype=torch.uint8, device=device)
-        self.back = torch.empty((T_cap * topk, H), dtype=torch.float16, device=device)
-        self.counts = torch.empty(2 * G, dtype=torch.int32, device=device)
+        self.exp_ws = pkg.moe_workspace(n, H, I, E // G, 1, device=device)
+        self.send = torch.empty((n, self.record_bytes), dtype=torch.uint8, device=device)
+        self.recv = torch.empty((n, self.record_bytes), dtype=torch.uint8, device=device)
+        self.back = torch.empty((n, H), dtype=torch.float16, device=device)
+        self.counts = torch.zeros(2 * G, dtype=torch.int32, device=device)
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
 
     def dispatch(self, x, ids, weights, in_gscale=None, in_amax=None):
         T = x.shape[0]
         if T > self.T_cap:
             raise ValueError(f"{T} tokens exceed the capacity {self.T_cap}")
         self.T = T
-        self.pkg.ep_dispatch(x, ids, weights, self.E, self.G, self.src_ws, self.send, self.counts[:self.G],
-                             in_gscale=in_gscale, in_amax=in_amax)
+        self.pkg.ep_dispatch(x, ids, weights, self.E, self.G, self.capacity, self.src_ws, self.send,
+                             self.counts[:self.G], self.overflow, in_gscale=in_gscale, in_amax=in_amax)
         return self.counts[:self.G], self.counts[self.G:]
 
-    def expert(self, records, n: int):
-        return self.pkg.ep_expert_forward(records, n, self.n_cap, self.experts, self.exp_ws)
+    def expert(self, records, recv_counts):
+        return self.pkg.ep_expert_forward(records, self.G, self.capacity, recv_counts, self.experts, self.exp_ws)
 
     def combine(self, back, out, accumulate: bool):
         return self.pkg.ep_combine(back, self.T, self.topk, self.E, self.src_ws, out, accumulate=accumulate)
@@ -67,25 +78,33 @@ class ExpertParallelMoE:
         if self.G > 1 and dist.get_world_size(group) != self.G:
             raise ValueError("ops were built for a different group size")
 
-    def forward(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False):
+    def forward(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False, mark=None):
+        """out[t] (+)= the layer's output for token t.  `mark(name)`, if given, is called around the expert-side
+        kernels ("kernel" / "kernel_end") so a caller can time them with events on the current stream."""
         ops, G, grp = self.ops, self.G, self.group
         send_counts, recv_counts = ops.dispatch(x, ids, weights, in_gscale=in_gscale, in_amax=in_amax)
         if G > 1:
             dist.all_to_all_single(recv_counts, send_counts, group=grp)
+            dist.all_to_all_single(ops.recv, ops.send, group=grp)
+            recv = ops.recv
         else:
             recv_counts.copy_(send_counts)
-        counts = ops.counts.tolist()                         # the split sizes: one device->host read per layer
-        sc, rc = counts[:G], counts[G:]
-        n_send, n_recv = sum(sc), sum(rc)
+            recv = ops.send
+        if mark is not None:
+            mark("kernel")
+        rows = ops.expert(recv, recv_counts)
+        if mark is not None:
+            mark("kernel_end")
         if G > 1:
-            recv = ops.recv[:n_recv]
-            dist.all_to_all_single(recv, ops.send[:n_send], output_split_sizes=rc, input_split_sizes=sc, group=grp)
-        else:
-            recv = ops.send[:n_send]
-        rows = ops.expert(recv, n_recv)
-        if G > 1:
-            back = ops.back[:n_send]
-            dist.all_to_all_single(back, rows, output_split_sizes=sc, input_split_sizes=rc, group=grp)
+            dist.all_to_all_single(ops.back, rows, group=grp)
+            back = ops.back
         else:
             back = rows
         return ops.combine(back, out, accumulate)
+
+    def overflowed(self, reset: bool = True) -> bool:
+        """True if a layer since the last reset had more than `capacity` records for one rank pair (host read)."""
+        v = bool(self.ops.overflow.item())
+        if reset:
+            self.ops.overflow.zero_()
+        return v

@@ -215,34 +215,39 @@ int nvfp4b_moe_pack_expert(const uint8_t* gate, const uint8_t* gate_scales, cons
 
 /* ---- expert parallelism: E experts sharded over G ranks, E/G consecutive experts per rank -------------------------
  *
- * One MoE layer on G ranks (the collectives are the caller's, e.g. NCCL all-to-all over NVLink):
- *   source rank:  nvfp4b_moe_route -> nvfp4b_ep_dispatch (records sorted by destination rank, per-rank counts)
- *   collectives:  all-to-all of the counts, then of the records (count[d] records of nvfp4b_ep_record_bytes(H))
- *   expert rank:  nvfp4b_ep_expert_forward on the received records (its E/G local experts)
- *   collectives:  all-to-all of the weighted output rows (fp16 [n, H], the workspace view's y) back to the sources
+ * One MoE layer on G ranks (the collectives are the caller's, e.g. NCCL all-to-all over NVLink).  Records travel in
+ * fixed slots, `capacity` per (source, destination) pair, so no step needs the counts on the host (a layer can be
+ * captured in a CUDA graph):
+ *   source rank:  nvfp4b_moe_route -> nvfp4b_ep_dispatch (records [G][capacity], per-rank counts)
+ *   collectives:  all-to-all of the counts (G ints) and of the record slots (capacity records per rank pair)
+ *   expert rank:  nvfp4b_ep_expert_forward on the received slots (its E/G local experts)
+ *   collectives:  all-to-all of the output row slots (fp16 [G * capacity, H], the workspace view's y) back
  *   source rank:  nvfp4b_ep_combine (slot-ordered sum into out; bit-identical to nvfp4b_moe_forward at G = 1).
  * A record carries the token's e2m1 codes, its logical e4m3 scales, the destination-local expert, the router weight
- * and the activation global scale the codes were made with (ranks quantise with their own dynamic scale). */
+ * and the activation global scale the codes were made with (ranks quantise with their own dynamic scale).  A rank
+ * pair with more than `capacity` records sets *overflow (the excess is dropped): capacity = T * topk can never
+ * overflow; a smaller one trades all-to-all bytes for a check of the flag after the step. */
 
 /* Bytes of one record: H/2 + H/16 + 16 (H % 256 == 0), 0 otherwise. */
 size_t nvfp4b_ep_record_bytes(int H);
 
-/* Source side: plans and packs the T*topk assignments (ids in [0, E), E % G == 0) as records into `records`
- * (T*topk slots), destination rank d's run first-to-last in rank order; send_counts[G] (device int32) receives the
- * per-rank record counts.  workspace: nvfp4b_moe_workspace_bytes(T, H, 32, E, topk); keep it until
- * nvfp4b_ep_combine (it holds each assignment's record slot). */
+/* Source side: plans and packs the T*topk assignments (ids in [0, E), E % G == 0) into `records` (G * capacity
+ * slots of nvfp4b_ep_record_bytes(H); destination d's records are slots [d * capacity, d * capacity + count)),
+ * send_counts[G] (device int32) = per-destination counts (at most capacity), *overflow |= 1 if any pair exceeds
+ * capacity.  workspace: nvfp4b_moe_workspace_bytes(T, H, 32, E, topk); keep it until nvfp4b_ep_combine. */
 int nvfp4b_ep_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E, int G,
-                       float in_gscale, const float* d_in_amax, void* workspace, uint8_t* records, int* send_counts,
-                       void* stream);
+                       int capacity, float in_gscale, const float* d_in_amax, void* workspace, uint8_t* records,
+                       int* send_counts, int* overflow, void* stream);
 
-/* Expert side: n received records (n <= n_cap) through the local experts (experts->num_experts = E/G): the weighted
- * fp16 output row of record i is left at row i of the workspace's y.  workspace:
- * nvfp4b_moe_workspace_bytes(n_cap, H, I, E/G, 1). */
-int nvfp4b_ep_expert_forward(const uint8_t* records, int n, int n_cap, const nvfp4b_moe_experts* experts,
-                             void* workspace, void* stream);
+/* Expert side: the G * capacity received record slots (slot s * capacity + j is a record iff j < recv_counts[s],
+ * recv_counts on the device) through the local experts (experts->num_experts = E/G): the weighted fp16 output row
+ * of slot i is left at row i of the workspace's y.  workspace: nvfp4b_moe_workspace_bytes(G * capacity, H, I,
+ * E/G, 1). */
+int nvfp4b_ep_expert_forward(const uint8_t* records, int G, int capacity, const int* recv_counts,
+                             const nvfp4b_moe_experts* experts, void* workspace, void* stream);
 
 /* Source side: out[t] (+)= sum over slots j, in order, of y_back[record slot of (t, j)], fp32 accumulation;
- * y_back holds the returned rows in this rank's record order.  flags: NVFP4B_MOE_ACCUMULATE or 0. */
+ * y_back holds the returned row slots in this rank's record-slot order.  flags: NVFP4B_MOE_ACCUMULATE or 0. */
 int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk, int E, const void* workspace, float* out,
                       int flags, void* stream);
 

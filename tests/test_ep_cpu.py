@@ -34,33 +34,43 @@ def routing(rank: int):
 
 
 class OracleOps:
-    """float64 CPU stand-in with KernelOps' interface and record order (destination rank, expert, token order)."""
+    """float64 CPU stand-in with KernelOps' interface: records in destination-major fixed slots (capacity =
+    T * topk per destination), each destination's records in expert order, token order inside an expert."""
 
     def __init__(self, rank: int, G: int):
         self.rank, self.G, self.topk, self.E = rank, G, TOPK, E
+        self.C = T * TOPK
         self.counts = torch.zeros(2 * G, dtype=torch.int32)
-        self.recv = torch.empty((G * T * TOPK, H + 2), dtype=torch.float64)
-        self.back = torch.empty((T * TOPK, H), dtype=torch.float64)
+        self.send = torch.zeros((G * self.C, H + 2), dtype=torch.float64)
+        self.recv = torch.zeros_like(self.send)
+        self.back = torch.zeros((G * self.C, H), dtype=torch.float64)
 
     def dispatch(self, x, ids, weights, in_gscale=None, in_amax=None):
         x, ids, weights = x.numpy(), ids.numpy(), weights.numpy()
+        el = E // self.G
         a = np.argsort(ids.reshape(-1), kind="stable")              # expert order, token order inside an expert
-        self.pos = np.empty_like(a)
-        self.pos[a] = np.arange(a.size)
         e = ids.reshape(-1)[a]
-        rec = np.concatenate([x[a // TOPK], (e % (E // self.G))[:, None], weights.reshape(-1)[a][:, None]], 1)
-        self.send = torch.from_numpy(rec)
+        d = e // el
+        per_rank = np.bincount(d, minlength=self.G)
+        starts = np.concatenate([[0], np.cumsum(per_rank)[:-1]])
+        slot = d * self.C + (np.arange(a.size) - starts[d])
+        self.slot = np.empty_like(a)
+        self.slot[a] = slot
+        rec = np.concatenate([x[a // TOPK], (e % el)[:, None], weights.reshape(-1)[a][:, None]], 1)
+        self.send.zero_()
+        self.send[torch.from_numpy(slot)] = torch.from_numpy(rec)
         self.T = x.shape[0]
-        per_rank = np.bincount(e // (E // self.G), minlength=self.G)
         self.counts[:self.G] = torch.from_numpy(per_rank.astype(np.int32))
         return self.counts[:self.G], self.counts[self.G:]
 
-    def expert(self, records, n):
-        r = records[:n].numpy()
-        out = np.zeros((n, H))
-        for i in range(n):
-            e = self.rank * (E // self.G) + int(r[i, H])
-            out[i] = r[i, H + 1] * expert_fn(e, r[i:i + 1, :H])[0]
+    def expert(self, records, recv_counts):
+        r = records.numpy()
+        out = np.zeros((r.shape[0], H))
+        for s in range(self.G):
+            for j in range(int(recv_counts[s])):
+                i = s * self.C + j
+                e = self.rank * (E // self.G) + int(r[i, H])
+                out[i] = r[i, H + 1] * expert_fn(e, r[i:i + 1, :H])[0]
         return torch.from_numpy(out)
 
     def combine(self, back, out, accumulate):
@@ -68,7 +78,7 @@ class OracleOps:
         res = np.zeros((self.T, H))
         for t in range(self.T):
             for j in range(TOPK):
-                res[t] += b[self.pos[t * TOPK + j]]
+                res[t] += b[self.slot[t * TOPK + j]]
         out.copy_(torch.from_numpy(res) + (out if accumulate else 0))
         return out
 

@@ -39,44 +39,55 @@ def test_ep_single_rank_bit_identical_to_moe_forward():
     assert torch.equal(out2, ref2)                      # same order: out, then the slots in order
 
 
+def _emulate(p, P, G, T, capacity=None):
+    """G ranks on one GPU: each rank's slots are exchanged by copies (what the all-to-all does)."""
+    import gemma_cuda_server_b200.expert_parallel as epm
+    E, k = P["E"], P["topk"]
+    ops = [epm.KernelOps(p, P["arena"].slice(r * E // G, (r + 1) * E // G), E, k, T_cap=T, G=G, capacity=capacity)
+           for r in range(G)]
+    C = ops[0].capacity
+    xs = [P["x"][r * T:(r + 1) * T].contiguous() for r in range(G)]
+    ids = [P["ids"][r * T:(r + 1) * T].contiguous() for r in range(G)]
+    ws = [P["w"][r * T:(r + 1) * T].contiguous() for r in range(G)]
+    amaxes = [p.amax(x) for x in xs]
+    for r in range(G):
+        ops[r].dispatch(xs[r], ids[r], ws[r], in_amax=amaxes[r])
+    for d in range(G):
+        for s in range(G):
+            ops[d].counts[G + s] = ops[s].counts[d]
+            ops[d].recv[s * C:(s + 1) * C].copy_(ops[s].send[d * C:(d + 1) * C])
+    rows = [ops[d].expert(ops[d].recv, ops[d].counts[G:]).clone() for d in range(G)]
+    for s in range(G):
+        for d in range(G):
+            ops[s].back[d * C:(d + 1) * C].copy_(rows[d][s * C:(s + 1) * C])
+    outs = []
+    for r in range(G):
+        out = torch.full((T, P["H"]), float("nan"), device="cuda")
+        ops[r].combine(ops[r].back, out, False)
+        outs.append(out)
+    torch.cuda.synchronize()
+    return ops, xs, ids, ws, amaxes, outs
+
+
 @pytest.mark.parametrize("G", [2, 4])
 def test_ep_emulated_ranks_bit_identical(G):
     T = 96
     p, P = make_problem(T * G, 512, 128, 32, 8, seed=43)
-    ids_all, w_all, _, _ = route_and_calibrate(p, P)
-    import gemma_cuda_server_b200.expert_parallel as epm
-    E, k = P["E"], P["topk"]
-    ops = [epm.KernelOps(p, P["arena"].slice(r * E // G, (r + 1) * E // G), E, k, T_cap=T, G=G) for r in range(G)]
-    xs = [P["x"][r * T:(r + 1) * T].contiguous() for r in range(G)]
-    ids = [ids_all[r * T:(r + 1) * T].contiguous() for r in range(G)]
-    ws = [w_all[r * T:(r + 1) * T].contiguous() for r in range(G)]
-    amaxes = [p.amax(x) for x in xs]
-    counts = []
-    for r in range(G):
-        sc, _ = ops[r].dispatch(xs[r], ids[r], ws[r], in_amax=amaxes[r])
-        counts.append(sc.tolist())
-    # records: source rank order inside every destination (all-to-all semantics)
-    recv_n = [sum(counts[s][d] for s in range(G)) for d in range(G)]
-    for d in range(G):
-        off = 0
-        for s in range(G):
-            start = sum(counts[s][:d])
-            n = counts[s][d]
-            ops[d].recv[off:off + n].copy_(ops[s].send[start:start + n])
-            off += n
-    rows = [ops[d].expert(ops[d].recv[:recv_n[d]], recv_n[d]).clone() for d in range(G)]
-    for s in range(G):
-        off_back = 0
-        for d in range(G):
-            n = counts[s][d]
-            src_off = sum(counts[q][d] for q in range(s))
-            ops[s].back[off_back:off_back + n].copy_(rows[d][src_off:src_off + n])
-            off_back += n
-    torch.cuda.synchronize()
+    P["ids"], P["w"], _, _ = route_and_calibrate(p, P)
+    ops, xs, ids, ws, amaxes, outs = _emulate(p, P, G, T)
     assert p.read_device_error() == 0
+    assert not any(int(o.overflow.item()) for o in ops)
     for r in range(G):
-        out = torch.full((T, P["H"]), float("nan"), device="cuda")
-        ops[r].combine(ops[r].back[:sum(counts[r])], out, False)
         ref = _ref(p, P, xs[r], ids[r], ws[r], amaxes[r])
         torch.cuda.synchronize()
-        assert torch.equal(out, ref), f"rank {r}: max diff {(out - ref).abs().max().item()}"
+        assert torch.equal(outs[r], ref), f"rank {r}: max diff {(outs[r] - ref).abs().max().item()}"
+
+
+def test_ep_overflow_is_flagged():
+    """A capacity below a rank pair's record count sets the overflow flag (the excess records are dropped)."""
+    G, T = 2, 64
+    p, P = make_problem(T * G, 512, 128, 32, 8, seed=47)
+    P["ids"], P["w"], _, _ = route_and_calibrate(p, P)
+    ops, *_ = _emulate(p, P, G, T, capacity=16)          # ~T*8/2 = 256 records per pair on average
+    assert all(int(o.overflow.item()) == 1 for o in ops)
+    assert all(int(c) <= 16 for o in ops for c in o.counts.tolist())
