@@ -1,26 +1,32 @@
 #!/usr/bin/env python
 """Benchmark of the B200 NVFP4 path; prints ONE JSON line (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload quant|gemm|moe] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ep|quant|gemm|moe] [--impl ours|reference]
 
-Workloads (synthetic seeded inputs with the configs' shapes and distributions):
-  quant (default)  cfg1 at its largest size: bf16 [8192, 2816] ~ N(0,1) with 0.1% x50 outliers.  One step = device
-                   global amax + NVFP4 quantise (codes, tile-layout e4m3 scales, fp32 amax).  Metric GB/s of
-                   algorithmic bytes T*K*(2 + 1/2 + 1/16) + 4.
-  moe              cfg3: one MoE layer, 4096 tokens, 128 experts, top-8: router + dispatch + grouped gate/up +
-                   grouped down with the weighted combine.  Metric tokens/s.
-  gemm             cfg2 at its largest size: M=8192, K=4096, N=14336, NVFP4 A and W resident, bf16 out with the
-                   fused global-scale multiply.  One step = one GEMM.  Metric TFLOP/s of 2*M*N*K.
-For N > 1 (torchrun, one process per GPU) every rank runs its own replica (the quantiser and the dense GEMM do not
-shard): value = sum over ranks of the work / the max over ranks of the device time.
+Workloads (synthetic seeded inputs and random-init weights with the configs' shapes):
+  ep (default)  cfg4: expert-parallel MoE stack on the N GPUs -- 30 MoE layers shaped as cfg3, 512 rows per GPU per
+                step, the 128 experts sharded 128/N per GPU, records and returned rows exchanged with NCCL
+                all-to-alls per layer; the step is replayed from one CUDA graph.  Metric tokens/s over all GPUs
+                (weak scaling: 512 rows per GPU at every N).
+  quant         cfg1 at its largest size: bf16 [8192, 2816] ~ N(0,1) with 0.1% x50 outliers.  One step = device
+                global amax + NVFP4 quantise (codes, tile-layout e4m3 scales, fp32 amax).  Metric GB/s of
+                algorithmic bytes T*K*(2 + 1/2 + 1/16) + 4.
+  moe           cfg3: one MoE layer, 4096 tokens, 128 experts, top-8: router + dispatch + grouped gate/up + grouped
+                down with the weighted combine.  Metric tokens/s.
+  gemm          cfg2 at its largest size: M=8192, K=4096, N=14336, NVFP4 A and W resident, bf16 out with the fused
+                global-scale multiply.  One step = one GEMM.  Metric TFLOP/s of 2*M*N*K.
+For N > 1 (torchrun, one process per GPU) quant, gemm and moe run one replica per rank (they do not shard):
+value = sum over ranks of the work / the max over ranks of the device time.
 
 Timing: W untimed warm-up steps; K timed steps, each bracketed by CUDA events on the launching stream; the L2 is
-flushed between steps outside the events (a 256 MiB write, then a 256 MiB read so no dirty lines remain); barrier + synchronize around the timed region; the max
-over ranks is taken.  `e2e` repeats the step through the public API from pinned host memory with the host->device
-copy of the inputs and the device->host copy of the outputs inside the timed region.
+flushed between steps outside the events (a 256 MiB write, then a 256 MiB read so no dirty lines remain); barrier +
+synchronize around the timed region; the max over ranks is taken.  `e2e` repeats the step through the public API
+from pinned host memory with the host->device copy of the inputs and the device->host copy of the outputs inside
+the timed region.
 
---impl reference times the reference's CPU implementation of the quantiser (the oracle's C port of
-scripts/nvfp4_ref.py:71-82, all host threads) on the same config; only rank 0 runs it.
+--impl reference times the reference's CPU implementation on the same config (rank 0 only): the quantiser (the
+oracle's C port of scripts/nvfp4_ref.py:71-82, all host threads) for quant, the MoE experts() semantics of
+scripts/ref_forward.py:160-192 (numpy, all host threads) for moe and ep.
 """
 from __future__ import annotations
 
@@ -50,7 +56,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep"], default="quant")
+    ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep"], default="ep")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
@@ -488,6 +494,71 @@ def cpu_cores():
         return os.cpu_count() or 1
 
 
+def run_reference_moe(args, world, orc):
+    """The reference's CPU MoE semantics (scripts/ref_forward.py:160-192: softmax top-8 router, per-token loop over
+    the selected experts, gelu_tanh(gate) * up, down, weighted sum) in W4A4 (x and h quantised with the NVFP4
+    quantiser port), numpy float32 matmuls on all host threads.  Experts are dequantised once when first used; each
+    step pushes a few tokens through one layer.  cfg4 (ep): tokens/s of the 30-layer stack = layer rate / 30."""
+    import numpy as np
+    import native
+    H, I, E, topk = 2816, 704, 128, 8
+    L = 30 if args.workload == "ep" else 1
+    S = 4                                                     # tokens per step (bounded sample)
+    rng = np.random.default_rng(7)
+    proj = rng.standard_normal((E, H)).astype(np.float32) * 0.02
+    experts = {}
+    for e in range(E):        # N(0, 0.02) weights, NVFP4-quantised (C port), dequantised once -- before timing
+        r = np.random.default_rng(1000 + e)
+        mats = []
+        for shape in ((2 * I, H), (H, I)):
+            bits = orc.f32_to_bf16_bits(r.standard_normal(shape).astype(np.float32) * 0.02)
+            g = orc.global_scale_from_amax(native.amax_bf16(bits))
+            pk, sf = native.quantize_bf16(bits, g)
+            mats.append(orc.dequantize(pk, sf, g).astype(np.float32))
+        experts[e] = (mats[0], mats[1], 2688.0 / 0.05)         # static h scale (calibrated order of magnitude)
+
+    def expert(e):
+        return experts[e]
+
+    def layer(x):
+        logits = x @ proj.T
+        p = np.exp(logits - logits.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        ids = np.argsort(-p, axis=1, kind="stable")[:, :topk]
+        w = np.take_along_axis(p, ids, 1)
+        w /= w.sum(1, keepdims=True)
+        gin = orc.global_scale_from_amax(np.abs(x).max())
+        _, _, xd = orc.quantize_rows(x.astype(np.float64), gin)
+        xd = xd.astype(np.float32)
+        out = np.zeros_like(x)
+        for t in range(x.shape[0]):
+            for j in range(topk):
+                w13, w2, gh = expert(int(ids[t, j]))
+                y = w13 @ xd[t]
+                h = orc.gelu_tanh(y[:I]) * y[I:]
+                _, _, hd = orc.quantize_rows(h[None].astype(np.float64), gh)
+                out[t] += w[t, j] * (w2 @ hd[0].astype(np.float32))
+        return out
+
+    xs = rng.standard_normal((S * (args.warmup + args.steps), H)).astype(np.float32)
+    for i in range(args.warmup):
+        layer(xs[i * S:(i + 1) * S])
+    t0 = time.perf_counter()
+    for i in range(args.warmup, args.warmup + args.steps):
+        layer(xs[i * S:(i + 1) * S])
+    el = time.perf_counter() - t0
+    val = S * args.steps / el / L
+    workload = ("cfg4 expert-parallel MoE stack" if L > 1 else "cfg3 MoE FFN layer")
+    sample = f"{S} tokens per step through one layer (E=128, top-8, H=2816, I=704); stack rate = layer rate / {L}"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload, "layers": L, "hidden": H, "experts": E, "inter": I, "topk": topk},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port", "sample": sample},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU quantiser (oracle C port, all host threads); rank 0 only."""
     if rank != 0:
@@ -495,8 +566,11 @@ def run_reference(args, rank, world):
     sys.path.insert(0, str(ROOT / "oracle"))
     import native
     import nvfp4_oracle as orc
+    if args.workload in ("moe", "ep"):
+        run_reference_moe(args, world, orc)
+        return
     if args.workload != "quant":
-        print(json.dumps({"impl": "reference", "unavailable": "reference CPU arm is timed for the quant workload"}))
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU arm is timed for the quant and MoE workloads"}))
         return
     T, K = 8192, 2816
     rows = 1024                               # bounded sample per step
