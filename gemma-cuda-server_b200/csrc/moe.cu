@@ -37,7 +37,7 @@ namespace nvfp4b {
 namespace {
 
 constexpr int kRouterSplits = 4;
-constexpr int kChunk = 1024;          // assignments per histogram / rank chunk
+constexpr int kChunk = 256;           // assignments per histogram / rank chunk (one rank round per CTA)
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -60,7 +60,8 @@ struct Workspace {
     int* row_assign;
     uint16_t* y;          // [T*topk, H] fp16 weighted expert outputs, assignment-major (deterministic combine)
     float* row_gscale;    // [max_rows] per-row activation global scale (expert-parallel rows come from many ranks)
-    int* ep_ids;          // [T*topk] expert-parallel: local expert of each received record
+    int* ep_ids;          // [T*topk] expert-parallel: local expert of each received record (expert side),
+                          //   record slot of each assignment (source side)
     float* ep_w;          // [T*topk] expert-parallel: router weight of each received record
     uint8_t* a_codes;
     uint8_t* a_scales;
@@ -599,41 +600,48 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hi
 }
 
 // Warp per token: quantise x[t] once (dynamic or static global scale), write one record per routed slot.
-// dest[a] on entry: compact position; on exit: the record slot d * capacity + (position - dst_start[d]), or -1
-// when that is past the capacity (overflowed, not sent).
+// kPackWarps warps per token, each quantising every kPackWarps-th run of 32 blocks of x[t] and writing them to all
+// of the token's records.  slot[a] = d * capacity + (dest[a] - dst_start[d]) for the assignment's destination d
+// (dest = compact expert-sorted position), or -1 past the capacity (overflowed, not sent).
+constexpr int kPackWarps = 4;
+
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
-                                                      int* __restrict__ dest, const int* __restrict__ ids,
+                                                      const int* __restrict__ dest, const int* __restrict__ ids,
                                                       const float* __restrict__ weights, int experts_per_rank,
                                                       int capacity, const int* __restrict__ dst_start,
                                                       float gscale, const float* __restrict__ d_amax,
-                                                      uint8_t* __restrict__ records) {
+                                                      uint8_t* __restrict__ records, int* __restrict__ slot) {
     const int lane = threadIdx.x & 31;
-    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int t = gw / kPackWarps, part = gw % kPackWarps;
     if (t >= T) return;
     const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
     const size_t rb = ep_record_bytes(H);
-    int my_dest = -1;
+    int my_slot = -1;
     if (lane < topk) {
         const long long a = (long long)t * topk + lane;
-        const int pos = dest[a];
+        const int pos = __ldg(dest + a);
         if (pos >= 0) {
             const int d = __ldg(ids + a) / experts_per_rank;
             const int i = pos - __ldg(dst_start + d);
-            my_dest = i < capacity ? d * capacity + i : -1;
+            my_slot = i < capacity ? d * capacity + i : -1;
         }
-        dest[a] = my_dest;
-    }
-    if (lane < topk && my_dest >= 0) {
-        EpMeta meta;
-        meta.expert = __ldg(ids + (long long)t * topk + lane) % experts_per_rank;
-        meta.weight = __ldg(weights + (long long)t * topk + lane);
-        meta.gscale = g;
-        meta.pad = 0;
-        *reinterpret_cast<EpMeta*>(records + (size_t)my_dest * rb + (H / 2) + (H / 16)) = meta;
+        if (part == 0) {
+            slot[a] = my_slot;
+            if (my_slot >= 0) {
+                EpMeta meta;
+                meta.expert = __ldg(ids + a) % experts_per_rank;
+                meta.weight = __ldg(weights + a);
+                meta.gscale = g;
+                meta.pad = 0;
+                *reinterpret_cast<EpMeta*>(records + (size_t)my_slot * rb + (H / 2) + (H / 16)) = meta;
+            }
+        }
     }
     const int kb = H >> 4;
     const uint16_t* xr = x + (long long)t * H;
-    for (int b = lane; b - lane < kb; b += 32) {
+    for (int b0 = part * 32; b0 < kb; b0 += 32 * kPackWarps) {
+        const int b = b0 + lane;
         uint32_t w0 = 0, w1 = 0, sf = 0;
         if (b < kb) {
             const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
             sf = quantize16_bf16(ww, g, w0, w1);
         }
         for (int j = 0; j < topk; ++j) {
-            const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
+            const int r = __shfl_sync(0xFFFFFFFFu, my_slot, j);
             if (r < 0 || b >= kb) continue;
             uint8_t* rec = records + (size_t)r * rb;
             *reinterpret_cast<uint2*>(rec + b * 8) = make_uint2(w0, w1);
@@ -688,35 +696,34 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
     if (lane == 0) row_gscale[r] = reinterpret_cast<const EpMeta*>(rec + (H / 2) + (H / 16))->gscale;
 }
 
-// out[t] (+)= sum_j y_back[dest[t*k + j]] in slot order (fp32 accumulation of the fp16 rows sent back).
+// out[t] (+)= sum_j y_back[slot[t*k + j]] in slot order (fp32 accumulation of the fp16 rows sent back).  One
+// thread per (token, 8 columns): T * H / 8 independent gathers.
 __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restrict__ y_back, int T, int H, int topk,
-                                                         const int* __restrict__ dest, float* __restrict__ out,
+                                                         const int* __restrict__ slot, float* __restrict__ out,
                                                          int accumulate) {
-    const int lane = threadIdx.x & 31;
-    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (t >= T) return;
-    const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
-    float* dst = out + (long long)t * H;
-    for (int c = lane * 8; c < H; c += 256) {
-        float acc[8];
-        if (accumulate) {
-            const float4 u = *reinterpret_cast<const float4*>(dst + c), v = *reinterpret_cast<const float4*>(dst + c + 4);
-            acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
-        } else {
+    const int chunks = H >> 3;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)T * chunks) return;
+    const int t = (int)(idx / chunks), c = (int)(idx - (long long)t * chunks) * 8;
+    float* dst = out + (long long)t * H + c;
+    float acc[8];
+    if (accumulate) {
+        const float4 u = *reinterpret_cast<const float4*>(dst), v = *reinterpret_cast<const float4*>(dst + 4);
+        acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
+    } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        }
-        for (int j = 0; j < topk; ++j) {
-            const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
-            if (r < 0) continue;
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(y_back + (long long)r * H + c));
-            const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
-            acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
-            acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
-        }
-        *reinterpret_cast<float4*>(dst + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        *reinterpret_cast<float4*>(dst + c + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     }
+    for (int j = 0; j < topk; ++j) {
+        const int r = __ldg(slot + (long long)t * topk + j);
+        if (r < 0) continue;
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y_back + (long long)r * H + c));
+        const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
+        acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+        acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+    }
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
 using GroupCfg = KCfg<256, 4, 1, 8>;
@@ -849,8 +856,9 @@ int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weight
                                      w.seg_start, send_counts, overflow);
     moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
                                              w.row_weight, w.row_assign);
-    ep_pack_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest, ids, weights,
-                                               E / G, capacity, w.seg_start, in_gscale, d_in_amax, records);
+    ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
+                                                            ids, weights, E / G, capacity, w.seg_start, in_gscale,
+                                                            d_in_amax, records, w.ep_ids);
     return launch_status();
 }
 
@@ -1189,7 +1197,8 @@ extern "C" int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk,
     if (flags & ~NVFP4B_MOE_ACCUMULATE) return NVFP4B_ERR_ARG;
     if (!aligned16(y_back) || !aligned16(out)) return NVFP4B_ERR_ALIGN;
     const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
-    ep_combine_kernel<<<(T + 7) / 8, 256, 0, (cudaStream_t)stream>>>(y_back, T, H, topk, w.dest, out,
-                                                                    (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0);
+    const long long threads = (long long)T * (H / 8);
+    ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0);
     return launch_status();
 }
