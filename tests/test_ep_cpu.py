@@ -1,6 +1,6 @@
 """Expert-parallel orchestration on CPU: two gloo ranks run ExpertParallelMoE (expert_parallel.py) with float64 stand-in
 ops (same record order, same per-expert function on both sides), and the result must equal the single-process
-layer over all experts.  This covers the collective steps (count exchange, uneven record all-to-all, return trip,
+layer over all experts.  This covers the collective steps (count exchange, fixed-slot record all-to-all, return trip,
 slot-ordered combine) without a GPU; the device ops are checked against the oracle in test_ep_gpu.py."""
 import os
 import socket
