@@ -58,6 +58,10 @@ def lib() -> ctypes.CDLL:
             "nvfp4b_gemm_set_tile_config": ([ctypes.c_int], ctypes.c_int),
             "nvfp4b_w4a16_gemm": ([_P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P],
                                   ctypes.c_int),
+            "nvfp4b_amax_f32": ([_P, ctypes.c_longlong, _P, _P], ctypes.c_int),
+            "nvfp4b_linear_workspace_bytes": ([ctypes.c_int, ctypes.c_int], ctypes.c_size_t),
+            "nvfp4b_linear": ([_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_float,
+                               ctypes.c_float, ctypes.c_int, _P, ctypes.c_size_t, _P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             f = getattr(L, name)
@@ -135,11 +139,12 @@ def fp4_gemv(y, wp, ws, w_gscale: float, x16, N: int, K: int, stream=None) -> No
 # ----------------------------------------------------------------------------------------------------------------
 
 def amax(x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    """max |x| of a bf16 tensor as a 1-element fp32 device tensor."""
-    assert x.dtype == torch.bfloat16 and x.is_cuda and x.is_contiguous()
+    """max |x| of a bf16 or fp32 tensor as a 1-element fp32 device tensor."""
+    assert x.dtype in (torch.bfloat16, torch.float32) and x.is_cuda and x.is_contiguous()
     if out is None:
         out = torch.empty(1, dtype=torch.float32, device=x.device)
-    _check("nvfp4b_amax_bf16", lib().nvfp4b_amax_bf16(_ptr(x), x.numel(), _ptr(out), _stream(stream)))
+    fn = lib().nvfp4b_amax_bf16 if x.dtype == torch.bfloat16 else lib().nvfp4b_amax_f32
+    _check("amax", fn(_ptr(x), x.numel(), _ptr(out), _stream(stream)))
     return out
 
 
@@ -180,6 +185,29 @@ def gemm(a, a_scales, a_dequant: float, b, b_scales, b_dequant: float, out: torc
     _check("gemm", lib().nvfp4b_gemm(_ptr(a), _ptr(a_scales), float(a_dequant), _ptr(a_amax), _ptr(b),
                                      _ptr(b_scales), float(b_dequant), M, N, K, _ptr(out), out_kind, ldd,
                                      _stream(stream)))
+    return out
+
+
+LINEAR_AUTO, LINEAR_W4A16, LINEAR_W4A4 = 0, 1, 2
+LINEAR_W4A4_MIN_M = 128
+
+
+def linear_workspace(M: int, K: int, device="cuda") -> torch.Tensor:
+    return torch.empty(int(lib().nvfp4b_linear_workspace_bytes(M, K)), dtype=torch.uint8, device=device)
+
+
+def linear(out, x, w, w_scales, w_scales_tiled, w_gscale: float, a_gscale: float | None = None,
+           mode: int = LINEAR_AUTO, workspace=None, stream=None) -> torch.Tensor:
+    """The reference's linear() (src/forward.cu:424-445): out[M, N] = x[M, K] @ W[N, K]^T, fp32 row-major in and
+    out, W = NVFP4 codes [N, K/2] with raw scales [N, K/16] (W4A16 path) and/or their tile-layout copy (W4A4 path).
+    a_gscale: static activation global scale; None = dynamic from the device amax of x."""
+    M, K = x.shape
+    N = w.shape[0]
+    if workspace is None:
+        workspace = linear_workspace(M, K, x.device)
+    _check("linear", lib().nvfp4b_linear(_ptr(out), _ptr(x), M, N, K, _ptr(w), _ptr(w_scales), _ptr(w_scales_tiled),
+                                         float(w_gscale), float(a_gscale or 0.0), mode, _ptr(workspace),
+                                         workspace.numel(), _stream(stream)))
     return out
 
 

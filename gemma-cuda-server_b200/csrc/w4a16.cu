@@ -81,7 +81,14 @@ __global__ void __launch_bounds__(256) w4a16_fast_kernel(float* __restrict__ out
     }
 }
 
-// Byte-granular path: any alignment, K % 16 == 0.
+// Value of one e2m1 code (sign in bit 3) by arithmetic, without the packed conversion instruction.
+__device__ __forceinline__ float e2m1_value(uint32_t c) {
+    const float m = e2m1_magnitude(c & 7u);
+    return (c & 8u) ? -m : m;
+}
+
+// Byte-granular path: any alignment of the codes and scales, 2-byte aligned activations, K % 16 == 0.  One
+// 16-element block per lane step; codes decoded by arithmetic.
 __global__ void __launch_bounds__(256) w4a16_bytes_kernel(float* __restrict__ out, const uint8_t* __restrict__ wp,
                                                           const uint8_t* __restrict__ ws, float inv_g,
                                                           const __half* __restrict__ x, int M, int N, int K) {
@@ -90,14 +97,18 @@ __global__ void __launch_bounds__(256) w4a16_bytes_kernel(float* __restrict__ ou
     if (n >= N) return;
     const uint8_t* wrow = wp + (size_t)n * (K / 2);
     const uint8_t* srow = ws + (size_t)n * (K / 16);
+    const int blocks = K / 16;
     for (int m = 0; m < M; ++m) {
         const __half* xr = x + (size_t)m * K;
         float acc = 0.f;
-        for (int k2 = lane; k2 < K / 2; k2 += 32) {
-            const float s = e4m3_to_float(srow[k2 >> 3]) * inv_g;
-            const float2 f = e2m1x2_to_float2(wrow[k2]);
-            acc = fmaf(f.x * s, __half2float(xr[2 * k2]), acc);
-            acc = fmaf(f.y * s, __half2float(xr[2 * k2 + 1]), acc);
+        for (int b = lane; b < blocks; b += 32) {
+            const float s = e4m3_to_float(srow[b]) * inv_g;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t c = wrow[8 * b + j];
+                acc = fmaf(e2m1_value(c & 0xFu) * s, __half2float(xr[16 * b + 2 * j]), acc);
+                acc = fmaf(e2m1_value(c >> 4) * s, __half2float(xr[16 * b + 2 * j + 1]), acc);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
@@ -109,6 +120,7 @@ int w4a16(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, cons
           cudaStream_t s) {
     if (!out || !wp || !ws || !x16) return NVFP4B_ERR_NULL;
     if (M <= 0 || N <= 0 || K <= 0 || (K & 15)) return NVFP4B_ERR_SHAPE;
+    if (reinterpret_cast<uintptr_t>(x16) & 1u) return NVFP4B_ERR_ALIGN;
     const float inv_g = 1.0f / w_gscale;
     const dim3 grid((N + 7) / 8);
     const bool fast = (K % 32 == 0) && aligned16(wp) && aligned16(x16) && ((reinterpret_cast<uintptr_t>(ws) & 1) == 0);

@@ -102,10 +102,38 @@ int nvfp4b_read_device_error(int reset);
 
 /* out[M, N] (fp32 row-major) = x16[M, K] (fp16 row-major) @ dequant(W[N, K])^T with raw, unswizzled weight codes
  * wp [N, K/2] and e4m3 scales ws [N, K/16]; dequant = code * e4m3 / w_gscale.  K % 16 == 0; any M (the
- * reference's kernel is limited to M <= 16).  16-byte aligned operands with K % 32 == 0 take the vectorised path,
- * anything else a byte-granular one. */
+ * reference's kernel is limited to M <= 16); x16 2-byte aligned.  16-byte aligned operands with K % 32 == 0 take
+ * the vectorised path, anything else a byte-granular one. */
 int nvfp4b_w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16,
                       int M, int N, int K, void* stream);
+
+/* ---- Dense Linear (the call site of src/forward.cu:424-445, linear()) ----------------------------------------- */
+
+/* d_amax[0] = max |x| over n fp32 values (16-byte aligned); zeroes d_amax first, then one reduction kernel. */
+int nvfp4b_amax_f32(const float* x, long long n, float* d_amax, void* stream);
+
+enum nvfp4b_linear_mode {
+    NVFP4B_LINEAR_AUTO = 0,   /* W4A4 when M >= NVFP4B_LINEAR_W4A4_MIN_M (prefill), W4A16 otherwise (decode) */
+    NVFP4B_LINEAR_W4A16 = 1,  /* fp16 activations x dequantised weights, fp32 accumulate (the reference's path) */
+    NVFP4B_LINEAR_W4A4 = 2    /* activations quantised to NVFP4, tcgen05 NVFP4 GEMM */
+};
+#define NVFP4B_LINEAR_W4A4_MIN_M 128
+
+/* Device bytes of the workspace nvfp4b_linear needs for an [M, K] input (caller allocates, 16-byte aligned). */
+size_t nvfp4b_linear_workspace_bytes(int M, int K);
+
+/* out[M, N] (fp32 row-major, ld N) = in[M, K] (fp32 row-major) @ W[N, K]^T with W in NVFP4: codes w [N, K/2],
+ * dequant code * e4m3 / w_gscale.  The W4A16 path reads the raw scales w_scales [N, K/16] (as the reference's
+ * Linear does); the W4A4 path reads the tile-layout copy w_scales_tiled (nvfp4b_scale_buffer_bytes(N, K), made
+ * once at load, like Model::wscale in src/forward.cu:369-376) and quantises `in` with the activation global scale
+ * a_gscale (static, compressed-tensors form 2688/amax), or, if a_gscale <= 0, with the dynamic scale of the
+ * device amax of `in`.  Only the pointer the chosen path reads may be NULL otherwise.  The W4A4 path needs
+ * K % 32 == 0.  Results: W4A4 = the oracle's float64 dequant-matmul of the quantised operands within fp32
+ * accumulation error; W4A16 = the fp16 activations times the dequantised weights in fp32.  No allocation, no
+ * synchronisation (capture-safe). */
+int nvfp4b_linear(float* out, const float* in, int M, int N, int K, const uint8_t* w, const uint8_t* w_scales,
+                  const uint8_t* w_scales_tiled, float w_gscale, float a_gscale, int mode, void* workspace,
+                  size_t workspace_bytes, void* stream);
 
 /* ---- MoE top-k grouped expert FFN (replaces the router and expert kernels of src/forward.cu:193-321 and the
  *      orchestration of moe(), src/forward.cu:516-553) ------------------------------------------------------------

@@ -84,4 +84,6 @@ def ref_lib():
         _ref.ref_nvfp4_gemm.argtypes = [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_float,
                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, _P]
         _ref.ref_nvfp4_gemm.restype = ctypes.c_int
+        _ref.ref_w4a16_gemm.argtypes = [_P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P]
+        _ref.ref_fp4_gemv.argtypes = [_P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int, _P]
     return _ref

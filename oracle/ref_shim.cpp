@@ -1,6 +1,6 @@
 // C entry points forwarding to the reference's own C++ functions (compiled from its unmodified sources by
 // oracle/build.py).  TEST INFRASTRUCTURE ONLY: lets the tests call the reference's host swizzle, its CUDA
-// quantiser and its cuBLASLt NVFP4 GEMM through ctypes.
+// quantiser, its cuBLASLt NVFP4 GEMM and its W4A16 kernels through ctypes.
 #include "fp4_gemm.h"
 #include "nvfp4_quant.h"
 
@@ -29,6 +29,16 @@ int ref_nvfp4_gemm(float* dD, const uint8_t* dA, const uint8_t* dAs, float ag, c
         if (cudaMalloc(&g_ws, kWsBytes) != cudaSuccess) return -201;
     }
     return nvfp4_gemm(dD, dA, dAs, ag, dB, dBs, bg, M, N, K, g_lt, g_ws, kWsBytes, (cudaStream_t)stream);
+}
+
+void ref_w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16, int M,
+                    int N, int K, void* stream) {
+    w4a16_gemm(out, wp, ws, w_gscale, x16, M, N, K, (cudaStream_t)stream);
+}
+
+void ref_fp4_gemv(float* y, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16, int N, int K,
+                  void* stream) {
+    fp4_gemv(y, wp, ws, w_gscale, x16, N, K, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -79,3 +79,23 @@ def test_argument_errors_need_no_gpu(built):
     assert L.nvfp4b_quantize_bf16(8, 4, 32, 1.0, None, 16, 16, None) == -2           # misaligned x
     assert L.nvfp4b_gemm(16, 16, 1.0, None, 16, 16, 1.0, 4, 4, 48, 16, 0, 4, None) == -1   # K % 32
     assert L.nvfp4b_gemm(16, 16, 1.0, None, 16, 16, 1.0, 4, 4, 64, 16, 9, 4, None) == -7   # out kind
+
+
+def test_linear_workspace_and_argument_errors_need_no_gpu(built):
+    pkg = load_package()
+    L = pkg.lib()
+    r = lambda b: (b + 255) // 256 * 256
+    for M, K in [(1, 2816), (128, 2816), (4096, 2112)]:
+        w4a4 = r(M * K // 2) + r(pkg.nvfp4_scale_buffer_bytes(M, K))
+        assert L.nvfp4b_linear_workspace_bytes(M, K) == 256 + max(w4a4, r(M * K * 2))
+    big = 1 << 40
+    assert L.nvfp4b_linear(None, 16, 4, 4, 64, 16, 16, 16, 1.0, 1.0, 0, 16, big, None) == -3      # out NULL
+    assert L.nvfp4b_linear(16, 16, 4, 4, 24, 16, 16, 16, 1.0, 1.0, 0, 16, big, None) == -1        # K % 16
+    assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, 16, 16, 1.0, 1.0, 0, 16, 64, None) == -1         # workspace size
+    assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, 16, 16, 1.0, 1.0, 7, 16, big, None) == -7        # mode
+    assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, 16, 16, 0.0, 1.0, 0, 16, big, None) == -1        # w_gscale <= 0
+    assert L.nvfp4b_linear(16, 8, 4, 4, 64, 16, 16, 16, 1.0, 1.0, 0, 16, big, None) == -2         # misaligned in
+    assert L.nvfp4b_linear(16, 16, 4, 4, 48, 16, 16, 16, 1.0, 1.0, 2, 16, big, None) == -1        # W4A4: K % 32
+    assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, 16, None, 1.0, 1.0, 2, 16, big, None) == -3      # W4A4: no tiles
+    assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, None, 16, 1.0, 1.0, 1, 16, big, None) == -3      # W4A16: no raw
+    assert L.nvfp4b_amax_f32(8, 16, 16, None) == -2
