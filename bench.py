@@ -58,6 +58,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep"], default="ep")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ep-exchange", choices=["auto", "p2p", "nccl"], default="auto",
+                    help="ep: records/rows stored over NVLink peer memory by the kernels (p2p), NCCL all-to-all "
+                         "(nccl), or auto = p2p on 2+ GPUs and the local path (no exchange at all) on 1")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
     return ap.parse_args()
@@ -388,10 +391,17 @@ class EpWorkload:
     unit = "tokens/s"
     dtype = "nvfp4"
 
-    def __init__(self, pkg, torch, orc, rank=0, world=1, group=None, T=512, H=2816, I=704, E=128, topk=8, L=30):
+    def __init__(self, pkg, torch, orc, rank=0, world=1, group=None, T=512, H=2816, I=704, E=128, topk=8, L=30,
+                 exchange="p2p"):
         import numpy as np
         import gemma_cuda_server_b200.expert_parallel as epm
         self.pkg, self.torch = pkg, torch
+        self.exchange = exchange
+        self.ex = None
+        if exchange == "p2p":       # one set of exchange buffers serves every layer (per-layer epochs)
+            C = epm.P2PKernelOps.default_capacity(T, topk, world)
+            self.ex = (epm.PeerExchange.create(pkg, world, C, H, group) if world > 1
+                       else epm.PeerExchange.local_group(pkg, 1, C, H)[0])
         self.T, self.H, self.I, self.E, self.topk, self.L, self.G = T, H, I, E, topk, L, world
         El = E // world
         gen = torch.Generator(device="cuda").manual_seed(4000 + rank)
@@ -418,7 +428,8 @@ class EpWorkload:
             pkg.quantize(w2, gscale=g2, packed=arena.w2.view(El * H, I // 2), scales=arena.w2_scales.view(-1))
             del w2
             arena.w2_gscale.fill_(g2)
-            ops = epm.KernelOps(pkg, arena, E, topk, T_cap=T, G=world)
+            ops = (epm.P2PKernelOps(pkg, arena, E, topk, T, self.ex) if exchange == "p2p"
+                   else epm.KernelOps(pkg, arena, E, topk, T_cap=T, G=world))
             Ld = dict(proj=proj, arena=arena, ops=ops, layer=epm.ExpertParallelMoE(ops, group),
                       amax=torch.zeros(1, device="cuda"), ids=torch.empty((T, topk), dtype=torch.int32, device="cuda"),
                       w=torch.empty((T, topk), dtype=torch.float32, device="cuda"))
@@ -442,7 +453,10 @@ class EpWorkload:
         self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
         self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_per_gpu": T, "hidden": H,
                        "experts": E, "experts_per_gpu": El, "inter": I, "topk": topk,
-                       "exchange": "NCCL all-to-all of NVFP4 records and fp16 rows per layer",
+                       "exchange": ("NVFP4 records and fp16 rows stored to peer memory over NVLink by the pack kernel "
+                                    "and the down-GEMM epilogue, per-layer flags (no collective)") if exchange == "p2p"
+                       else ("none (one GPU holds every expert)" if world == 1
+                             else "NCCL all-to-all of NVFP4 records and fp16 rows per layer"),
                        "l2": "flushed between steps (256 MiB write + 256 MiB read)", "step_flops": self.step_flops}
 
     def step(self, mark=None):
@@ -473,6 +487,17 @@ class EpWorkload:
         else:
             self.step()
         self.h_out.copy_(self.res, non_blocking=True)
+
+    def received(self, li=0):
+        """Records this rank's experts ran in layer li's last run."""
+        if self.exchange == "p2p":
+            return sum(self.ex.recv_counts())        # one exchange for all layers: the last layer's counts
+        return int(self.layers[li]["ops"].counts[self.G:].sum().item())
+
+    def close(self):
+        if self.ex is not None:
+            self.ex.close()
+            self.ex = None
 
     def cpu_run(self, native, orc, seconds):
         """Layer 0 of the stack through the reference's experts() semantics (W4A4, dequantised experts, float32)
@@ -618,7 +643,8 @@ def main():
     pkg = load_package()
     pkg.lib()
     if args.workload == "ep":
-        W = EpWorkload(pkg, torch, orc, rank=rank, world=world)
+        exchange = args.ep_exchange if args.ep_exchange != "auto" else ("p2p" if world > 1 else "nccl")
+        W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange)
     else:
         W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload}[args.workload](pkg, torch, orc)
     # L2 flush between steps: write a 256 MiB buffer (evicts the step's data), then read another 256 MiB buffer so
@@ -744,7 +770,7 @@ def main():
                 "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
                 "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
     elif W.name == "ep":
-        n_recv = int(W.layers[0]["ops"].counts[W.G:].sum().item())   # records this rank's experts ran in layer 0
+        n_recv = W.received(len(W.layers) - 1)     # records this rank's experts ran (last layer of the last step)
         achieved = 2.0 * n_recv * 3 * W.I * W.H / kern_s / 1e12
         fp4_peak = peaks["bf16_tflops"] * 4.0
         roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
@@ -785,7 +811,11 @@ def main():
         W.graph = None
         graph = None
         torch.cuda.synchronize()
+    if W.name == "ep":                             # every rank done with every peer's buffers before they go
+        barrier()
+        W.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

@@ -478,3 +478,119 @@ def ep_combine(y_back, T: int, topk: int, E: int, workspace, out, accumulate: bo
         _ptr(y_back), T, H, topk, E, _ptr(workspace), _ptr(out), MOE_ACCUMULATE if accumulate else 0,
         _stream(stream)))
     return out
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# Expert parallelism over NVLink peer memory (include/nvfp4_b200.h: nvfp4b_ep_p2p_*, nvfp4b_ipc_*)
+# ----------------------------------------------------------------------------------------------------------------
+
+class EpPeers(ctypes.Structure):
+    """nvfp4b_ep_peers: this rank's view of every rank's exchange buffers (device pointers)."""
+    _fields_ = [("rank", ctypes.c_int), ("G", ctypes.c_int), ("capacity", ctypes.c_int),
+                ("recv", _P), ("back", _P), ("counts", _P), ("flags", _P),
+                ("my_recv", _P), ("my_back", _P), ("my_counts", _P), ("my_flags", _P), ("state", _P)]
+
+
+def _p2p_sigs():
+    L = _ep_sigs()
+    if getattr(L, "_p2p_ready", False):
+        return L
+    PP = ctypes.POINTER(EpPeers)
+    sig = {
+        "nvfp4b_ep_p2p_buffer_bytes": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, _P], ctypes.c_size_t),
+        "nvfp4b_ep_p2p_dispatch": ([_P, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_float, _P, _P, PP, _P, _P], ctypes.c_int),
+        "nvfp4b_ep_p2p_expert_forward": ([ctypes.POINTER(_Experts), _P, PP, _P], ctypes.c_int),
+        "nvfp4b_ep_p2p_combine": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, PP, _P,
+                                   ctypes.c_int, _P], ctypes.c_int),
+        "nvfp4b_ep_p2p_state": ([PP, _P], ctypes.c_int),
+        "nvfp4b_ep_p2p_recv_counts": ([PP, _P], ctypes.c_int),
+        "nvfp4b_ipc_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+        "nvfp4b_ipc_free": ([_P], ctypes.c_int),
+        "nvfp4b_ipc_handle": ([_P, _P], ctypes.c_int),
+        "nvfp4b_ipc_open": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+        "nvfp4b_ipc_close": ([_P], ctypes.c_int),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    L._p2p_ready = True
+    return L
+
+
+def ep_p2p_buffer_layout(G: int, capacity: int, H: int):
+    """(bytes, [offset of receive slots, return rows, counts, flags, state]) of one rank's exchange buffers."""
+    off = (ctypes.c_size_t * 5)()
+    n = int(_p2p_sigs().nvfp4b_ep_p2p_buffer_bytes(G, capacity, H, off))
+    if n == 0:
+        raise NvFp4Error("ep_p2p_buffer_bytes", -1)
+    return n, [int(v) for v in off]
+
+
+def ep_p2p_state(peers: EpPeers) -> list[int]:
+    """Debug read of a rank's 4 private words (synchronous)."""
+    out = (ctypes.c_uint * 4)()
+    _check("ep_p2p_state", _p2p_sigs().nvfp4b_ep_p2p_state(ctypes.byref(peers), out))
+    return list(out)
+
+
+def ep_p2p_recv_counts(peers: EpPeers) -> list[int]:
+    """Debug read of the records a rank received from each source in its last layer (synchronous)."""
+    out = (ctypes.c_int * peers.G)()
+    _check("ep_p2p_recv_counts", _p2p_sigs().nvfp4b_ep_p2p_recv_counts(ctypes.byref(peers), out))
+    return list(out)
+
+
+def ipc_alloc(nbytes: int) -> int:
+    p = ctypes.c_void_p()
+    _check("ipc_alloc", _p2p_sigs().nvfp4b_ipc_alloc(nbytes, ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_free(ptr: int) -> None:
+    _check("ipc_free", _p2p_sigs().nvfp4b_ipc_free(ptr))
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    _check("ipc_handle", _p2p_sigs().nvfp4b_ipc_handle(ptr, buf))
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    p = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), 64)
+    _check("ipc_open", _p2p_sigs().nvfp4b_ipc_open(buf, ctypes.byref(p)))
+    return int(p.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check("ipc_close", _p2p_sigs().nvfp4b_ipc_close(ptr))
+
+
+def ep_p2p_dispatch(x, ids, weights, E: int, workspace, peers: EpPeers, overflow, in_gscale: float | None = None,
+                    in_amax=None, stream=None) -> None:
+    """Source side over peer memory: records into the destination ranks' receive slots, flags raised."""
+    T, H = x.shape
+    topk = ids.shape[1]
+    _check("ep_p2p_dispatch", _p2p_sigs().nvfp4b_ep_p2p_dispatch(
+        _ptr(x), T, H, _ptr(ids), _ptr(weights), topk, E, float(in_gscale or 0.0), _ptr(in_amax), _ptr(workspace),
+        ctypes.byref(peers), _ptr(overflow), _stream(stream)))
+
+
+def ep_p2p_expert_forward(experts: MoeExperts, workspace, peers: EpPeers, stream=None) -> None:
+    """Expert side over peer memory: waits for the records, rows stored into the source ranks' return rows."""
+    ex = experts.struct()
+    _check("ep_p2p_expert_forward", _p2p_sigs().nvfp4b_ep_p2p_expert_forward(
+        ctypes.byref(ex), _ptr(workspace), ctypes.byref(peers), _stream(stream)))
+
+
+def ep_p2p_combine(T: int, topk: int, E: int, workspace, peers: EpPeers, out, accumulate: bool = False,
+                   stream=None):
+    """Source side over peer memory: waits for the rows, slot-ordered sum into out."""
+    H = out.shape[1]
+    _check("ep_p2p_combine", _p2p_sigs().nvfp4b_ep_p2p_combine(
+        T, H, topk, E, _ptr(workspace), ctypes.byref(peers), _ptr(out), MOE_ACCUMULATE if accumulate else 0,
+        _stream(stream)))
+    return out

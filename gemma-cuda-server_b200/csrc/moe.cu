@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -63,6 +64,7 @@ struct Workspace {
     int* ep_ids;          // [T*topk] expert-parallel: local expert of each received record (expert side),
                           //   record slot of each assignment (source side)
     float* ep_w;          // [T*topk] expert-parallel: router weight of each received record
+    int* ep_send;         // [256] expert-parallel over peer memory: records per destination rank (source side)
     uint8_t* a_codes;
     uint8_t* a_scales;
     uint8_t* h_codes;
@@ -93,6 +95,7 @@ Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     w.row_gscale = (float*)take((size_t)rows * 4);
     w.ep_ids = (int*)take((size_t)n_assign * 4);
     w.ep_w = (float*)take((size_t)n_assign * 4);
+    w.ep_send = (int*)take(256 * 4);
     w.a_codes = (uint8_t*)take((size_t)rows * (H / 2));
     w.a_scales = (uint8_t*)take(scale_bytes(rows, H));
     w.h_codes = (uint8_t*)take((size_t)rows * (I / 2));
@@ -358,6 +361,73 @@ __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* 
     }
 }
 
+// ---- peer-memory signalling (expert parallelism without a collective library) ---------------------------------
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+constexpr unsigned long long kPeerWaitNs = 10000000000ull;   // 10 s per flag, then the wait gives up
+
+// Per-rank private words (nvfp4b_ep_peers::state): the epoch of the current layer (advanced by the last block of
+// the layer's pack kernel, which publishes the layer's records with it), and the completion counters of the two
+// kernels that publish to other ranks.  Every flag of a layer carries its epoch.
+enum EpState : int { kEpEpoch = 0, kEpPackDone = 1, kEpDownDone = 2 };
+
+// Source-side publication arguments of ep_pack_kernel (recv == nullptr: local record slots, no publication).
+struct EpPackPeers {
+    uint8_t* const* recv;
+    int* const* counts;
+    unsigned* const* flags;
+    unsigned* state;
+    const int* send_counts;
+    int rank, G;
+};
+
+// Called by every thread of a block after its last store to peer memory.  The block barrier orders the block's
+// stores before thread 0's fence and arrival (GPU scope: the arriving blocks and the last one share the GPU); true
+// in every thread of the block that arrives last (the counter is reset for the next launch).  That block's
+// system-scope fence then orders every block's stores (cumulatively) before the release stores that follow it.
+__device__ __forceinline__ bool last_block_arrived(unsigned* counter) {
+    __shared__ unsigned s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(counter, 1u);
+        s_last = old == gridDim.x - 1 ? 1u : 0u;
+        if (s_last) {
+            *counter = 0u;
+            __threadfence_system();
+        }
+    }
+    __syncthreads();
+    return s_last != 0u;
+}
+
+// Thread 0 of a block: waits until flags[g] >= epoch for every g < G (acquire, system scope; bounded, a timeout is
+// recorded in *err and the wait ends); the block barrier then makes what the flags publish visible to the block.
+__device__ __forceinline__ void wait_peer_flags(const unsigned* flags, int G, unsigned epoch, int* err) {
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        for (int g = 0; g < G && ok; ++g) {
+            if ((int)(ld_acquire_sys(flags + g) - epoch) >= 0) continue;
+            const unsigned long long t0 = sm100::globaltimer();
+            while ((int)(ld_acquire_sys(flags + g) - epoch) < 0) {
+                if (sm100::globaltimer() - t0 > kPeerWaitNs) { ok = false; break; }
+                __nanosleep(64);
+            }
+        }
+        if (!ok) atomicCAS(err, 0, sm100::kErrTimeoutPeer);
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // 4./5. grouped GEMM epilogues
 // ---------------------------------------------------------------------------------------------------------------
@@ -468,8 +538,31 @@ struct DownEpi {
     const float* weights;
     const float* w2_gscale;
     const float* a2_gscale;
+    // Expert parallelism over peer memory (DETERMINISTIC only): the row of received slot a = s * capacity + j goes
+    // to source rank s's return rows, row rank * capacity + j, instead of y[a]; the last epilogue warp of the grid
+    // then raises the rows-landed flags (flags[s][G + rank]).
+    uint16_t* const* peer_back = nullptr;
+    unsigned* const* peer_flags = nullptr;
+    unsigned* state = nullptr;
+    int rank = 0, G = 0, capacity = 0;
 
-    __device__ __forceinline__ void finish() const {}
+    // Every epilogue warp (warps 4.. of every CTA) calls this once after its last tile.
+    __device__ __forceinline__ void finish() const {
+        if constexpr (DETERMINISTIC) {
+            if (!peer_back) return;
+            __syncwarp();
+            if ((threadIdx.x & 31) == 0) {
+                __threadfence();                         // arrival at GPU scope; the last warp fences system-wide
+                const unsigned total = gridDim.x * ((blockDim.x >> 5) - 4u);
+                if (atomicAdd(state + kEpDownDone, 1u) == total - 1u) {
+                    state[kEpDownDone] = 0u;
+                    __threadfence_system();
+                    const unsigned epoch = state[kEpEpoch];
+                    for (int g = 0; g < G; ++g) st_release_sys(peer_flags[g] + G + rank, epoch);
+                }
+            }
+        }
+    }
 
     // DETERMINISTIC: each warp transposes its 32-row x 32-column chunk through shared memory (32 x 33 floats) so
     // every store instruction writes four full 64-byte row segments of y instead of 32 scattered 8-byte pieces.
@@ -482,6 +575,10 @@ struct DownEpi {
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
             const int lane = threadIdx.x & 31;
+            uint16_t* rowp = nullptr;
+            if (a >= 0)
+                rowp = peer_back ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
+                                 : y + (long long)a * H;
             float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 4) * (32 * 33);   // epilogue warps are 4..
             const int sub = lane >> 3, q = (lane & 7) * 4;
 #pragma unroll
@@ -495,10 +592,11 @@ struct DownEpi {
 #pragma unroll
                 for (int g = 0; g < 8; ++g) {
                     const int i = 4 * g + sub;
-                    const int ai = __shfl_sync(0xFFFFFFFFu, a, i);
+                    uint16_t* pi = reinterpret_cast<uint16_t*>(
+                        __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), i));
                     const float* src = tile + i * 33 + q;
-                    if (ai >= 0)
-                        *reinterpret_cast<uint2*>(y + (long long)ai * H + n0 + q) =
+                    if (pi)
+                        *reinterpret_cast<uint2*>(pi + n0 + q) =
                             make_uint2(pack_half2_sat(src[0], src[1]), pack_half2_sat(src[2], src[3]));
                 }
             }
@@ -602,7 +700,9 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hi
 // Warp per token: quantise x[t] once (dynamic or static global scale), write one record per routed slot.
 // kPackWarps warps per token, each quantising every kPackWarps-th run of 32 blocks of x[t] and writing them to all
 // of the token's records.  slot[a] = d * capacity + (dest[a] - dst_start[d]) for the assignment's destination d
-// (dest = compact expert-sorted position), or -1 past the capacity (overflowed, not sent).
+// (dest = compact expert-sorted position), or -1 past the capacity (overflowed, not sent).  The record goes to
+// records[slot], or with peers.recv to peer d's receive slot rank * capacity + (slot - d * capacity); the last
+// block then stores the per-destination counts, raises the records-landed flags and advances the layer epoch.
 constexpr int kPackWarps = 4;
 
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
@@ -610,62 +710,81 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
                                                       const float* __restrict__ weights, int experts_per_rank,
                                                       int capacity, const int* __restrict__ dst_start,
                                                       float gscale, const float* __restrict__ d_amax,
-                                                      uint8_t* __restrict__ records, int* __restrict__ slot) {
+                                                      uint8_t* __restrict__ records, int* __restrict__ slot,
+                                                      const EpPackPeers peers) {
     const int lane = threadIdx.x & 31;
     const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int t = gw / kPackWarps, part = gw % kPackWarps;
-    if (t >= T) return;
-    const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
-    const size_t rb = ep_record_bytes(H);
-    int my_slot = -1;
-    if (lane < topk) {
-        const long long a = (long long)t * topk + lane;
-        const int pos = __ldg(dest + a);
-        if (pos >= 0) {
-            const int d = __ldg(ids + a) / experts_per_rank;
-            const int i = pos - __ldg(dst_start + d);
-            my_slot = i < capacity ? d * capacity + i : -1;
+    if (t < T) {
+        const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
+        const size_t rb = ep_record_bytes(H);
+        uint8_t* my_rec = nullptr;
+        if (lane < topk) {
+            const long long a = (long long)t * topk + lane;
+            const int pos = __ldg(dest + a);
+            int my_slot = -1;
+            if (pos >= 0) {
+                const int d = __ldg(ids + a) / experts_per_rank;
+                const int i = pos - __ldg(dst_start + d);
+                if (i < capacity) {
+                    my_slot = d * capacity + i;
+                    my_rec = peers.recv ? peers.recv[d] + ((size_t)peers.rank * capacity + i) * rb
+                                        : records + (size_t)my_slot * rb;
+                }
+            }
+            if (part == 0) {
+                slot[a] = my_slot;
+                if (my_rec) {
+                    EpMeta meta;
+                    meta.expert = __ldg(ids + a) % experts_per_rank;
+                    meta.weight = __ldg(weights + a);
+                    meta.gscale = g;
+                    meta.pad = 0;
+                    *reinterpret_cast<EpMeta*>(my_rec + (H / 2) + (H / 16)) = meta;
+                }
+            }
         }
-        if (part == 0) {
-            slot[a] = my_slot;
-            if (my_slot >= 0) {
-                EpMeta meta;
-                meta.expert = __ldg(ids + a) % experts_per_rank;
-                meta.weight = __ldg(weights + a);
-                meta.gscale = g;
-                meta.pad = 0;
-                *reinterpret_cast<EpMeta*>(records + (size_t)my_slot * rb + (H / 2) + (H / 16)) = meta;
+        const int kb = H >> 4;
+        const uint16_t* xr = x + (long long)t * H;
+        for (int b0 = part * 32; b0 < kb; b0 += 32 * kPackWarps) {
+            const int b = b0 + lane;
+            uint32_t w0 = 0, w1 = 0, sf = 0;
+            if (b < kb) {
+                const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
+                const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
+                const uint32_t ww[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                sf = quantize16_bf16(ww, g, w0, w1);
+            }
+            for (int j = 0; j < topk; ++j) {
+                uint8_t* rec = reinterpret_cast<uint8_t*>(
+                    __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(my_rec), j));
+                if (!rec || b >= kb) continue;
+                *reinterpret_cast<uint2*>(rec + b * 8) = make_uint2(w0, w1);
+                rec[(H / 2) + b] = (uint8_t)sf;
             }
         }
     }
-    const int kb = H >> 4;
-    const uint16_t* xr = x + (long long)t * H;
-    for (int b0 = part * 32; b0 < kb; b0 += 32 * kPackWarps) {
-        const int b = b0 + lane;
-        uint32_t w0 = 0, w1 = 0, sf = 0;
-        if (b < kb) {
-            const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
-            const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
-            const uint32_t ww[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-            sf = quantize16_bf16(ww, g, w0, w1);
+    if (peers.recv && last_block_arrived(peers.state + kEpPackDone)) {
+        const unsigned epoch = peers.state[kEpEpoch] + 1u;     // no other block reads it: all have arrived
+        for (int d = threadIdx.x; d < peers.G; d += blockDim.x) {
+            peers.counts[d][peers.rank] = peers.send_counts[d];
+            st_release_sys(peers.flags[d] + peers.rank, epoch);
         }
-        for (int j = 0; j < topk; ++j) {
-            const int r = __shfl_sync(0xFFFFFFFFu, my_slot, j);
-            if (r < 0 || b >= kb) continue;
-            uint8_t* rec = records + (size_t)r * rb;
-            *reinterpret_cast<uint2*>(rec + b * 8) = make_uint2(w0, w1);
-            rec[(H / 2) + b] = (uint8_t)sf;
-        }
+        __syncthreads();
+        if (threadIdx.x == 0) peers.state[kEpEpoch] = epoch;
     }
 }
 
 // Slot i = s * capacity + j holds a record iff j < recv_counts[s]; empty slots get expert -1 (skipped by the plan).
-__global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* __restrict__ records, int n, int H, int capacity,
-                                                      const int* __restrict__ recv_counts, int* __restrict__ ids,
-                                                      float* __restrict__ w) {
+// With wait_flags (exchange over peer memory) every block first waits for the records-landed flags of this layer.
+__global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* records, int n, int H, int capacity,
+                                                      const int* recv_counts, int* __restrict__ ids,
+                                                      float* __restrict__ w, const unsigned* wait_flags, int G,
+                                                      const unsigned* state, int* err) {
+    if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    if (i % capacity >= __ldg(recv_counts + i / capacity)) {
+    if (i % capacity >= recv_counts[i / capacity]) {
         ids[i] = -1;
         w[i] = 0.f;
         return;
@@ -697,10 +816,13 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
 }
 
 // out[t] (+)= sum_j y_back[slot[t*k + j]] in slot order (fp32 accumulation of the fp16 rows sent back).  One
-// thread per (token, 8 columns): T * H / 8 independent gathers.
-__global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restrict__ y_back, int T, int H, int topk,
+// thread per (token, 8 columns): T * H / 8 independent gathers.  With wait_flags (exchange over peer memory) every
+// block first waits for the rows-landed flags of this layer.
+__global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back, int T, int H, int topk,
                                                          const int* __restrict__ slot, float* __restrict__ out,
-                                                         int accumulate) {
+                                                         int accumulate, const unsigned* wait_flags, int G,
+                                                         const unsigned* state, int* err) {
+    if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err);
     const int chunks = H >> 3;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)T * chunks) return;
@@ -717,7 +839,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* __restr
     for (int j = 0; j < topk; ++j) {
         const int r = __ldg(slot + (long long)t * topk + j);
         if (r < 0) continue;
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(y_back + (long long)r * H + c));
+        const uint4 q = *reinterpret_cast<const uint4*>(y_back + (long long)r * H + c);
         const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
         acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
         acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
@@ -804,7 +926,7 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
 }
 
 int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, float* out, int flags,
-         const Workspace& w, cudaStream_t s) {
+         const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr) {
     const bool accumulate = (flags & NVFP4B_MOE_ACCUMULATE) != 0;
     const bool deterministic = (flags & NVFP4B_MOE_ATOMIC) == 0;
     const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
@@ -831,6 +953,14 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
     sc.k_tiles = cp.k_tiles;
     if (deterministic) {
         DownEpi<true> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
+        if (peers) {
+            e.peer_back = peers->back;
+            e.peer_flags = peers->flags;
+            e.state = peers->state;
+            e.rank = peers->rank;
+            e.G = peers->G;
+            e.capacity = peers->capacity;
+        }
         st = launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
         if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
         moe_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(w.y, T, H, topk, out, accumulate ? 1 : 0);
@@ -858,18 +988,49 @@ int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weight
                                              w.row_weight, w.row_assign);
     ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
                                                             ids, weights, E / G, capacity, w.seg_start, in_gscale,
-                                                            d_in_amax, records, w.ep_ids);
+                                                            d_in_amax, records, w.ep_ids, EpPackPeers{});
+    return launch_status();
+}
+
+// expert parallelism over peer memory, source side: as ep_dispatch, with the records stored into the destination
+// ranks' receive slots and the counts + records-landed flags published by the pack kernel.
+int ep_dispatch_p2p(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E,
+                    float in_gscale, const float* d_in_amax, const Workspace& w, const nvfp4b_ep_peers& pr,
+                    int* overflow, cudaStream_t s) {
+    const int G = pr.G, capacity = pr.capacity;
+    const int n_assign = T * topk;
+    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
+    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
+    ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, capacity, w.chunk_base, w.seg_count,
+                                     w.seg_start, w.ep_send, overflow);
+    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
+                                             w.row_weight, w.row_assign);
+    EpPackPeers pp;
+    pp.recv = pr.recv;
+    pp.counts = pr.counts;
+    pp.flags = pr.flags;
+    pp.state = pr.state;
+    pp.send_counts = w.ep_send;
+    pp.rank = pr.rank;
+    pp.G = G;
+    ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
+                                                            ids, weights, E / G, capacity, w.seg_start, in_gscale,
+                                                            d_in_amax, nullptr, w.ep_ids, pp);
     return launch_status();
 }
 
 // expert parallelism, expert side: received records -> padded expert-sorted operand -> gate/up -> down GEMM, leaving
 // each record's weighted output row (fp16) in w.y in record order.
 int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_counts, const nvfp4b_moe_experts* ex,
-              const Workspace& w, cudaStream_t s) {
+              const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr) {
     const int H = ex->hidden, E = ex->num_experts;
     const int n = G * capacity;
     const int n_chunks = (n + kChunk - 1) / kChunk;
-    ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, capacity, recv_counts, w.ep_ids, w.ep_w);
+    int* err = device_error_ptr();
+    if (!err) return NVFP4B_ERR_CUDA;
+    ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, capacity, recv_counts, w.ep_ids, w.ep_w,
+                                                   peers ? peers->my_flags : nullptr, G,
+                                                   peers ? peers->state : nullptr, err);
     moe_hist_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist);
     moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
                                       w.tile_expert);
@@ -884,7 +1045,7 @@ int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_count
     if (st) return st;
     st = gate_up<false>(ex, n, 1, 1.0f, nullptr, nullptr, w, s, true);
     if (st) return st;
-    return down(ex, n, 1, w.ep_w, nullptr, 0, w, s);
+    return down(ex, n, 1, w.ep_w, nullptr, 0, w, s, peers);
 }
 
 // Gate/up interleave: w13 row 32g + r <- gate row 16g + r; 32g + 16 + r <- up row 16g + r.
@@ -1199,6 +1360,132 @@ extern "C" int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk,
     const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
     const long long threads = (long long)T * (H / 8);
     ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0);
+        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, nullptr, 0, nullptr, nullptr);
     return launch_status();
+}
+
+// ---- expert parallelism over peer memory ---------------------------------------------------------------------
+
+static int check_peers(const nvfp4b_ep_peers* p) {
+    if (!p || !p->recv || !p->back || !p->counts || !p->flags || !p->my_recv || !p->my_back || !p->my_counts ||
+        !p->my_flags || !p->state)
+        return NVFP4B_ERR_NULL;
+    if (p->G <= 0 || p->G > 256 || p->rank < 0 || p->rank >= p->G || p->capacity <= 0 ||
+        (long long)p->G * p->capacity > (1 << 26))
+        return NVFP4B_ERR_SHAPE;
+    if (!aligned16(p->my_recv) || !aligned16(p->my_back)) return NVFP4B_ERR_ALIGN;
+    return NVFP4B_OK;
+}
+
+static size_t p2p_layout(int G, int capacity, int H, size_t* off) {
+    const size_t n = (size_t)G * capacity;
+    size_t o[5];
+    o[0] = 0;
+    o[1] = o[0] + align256(n * ep_record_bytes(H));
+    o[2] = o[1] + align256(n * (size_t)H * 2);
+    o[3] = o[2] + align256((size_t)G * 4);
+    o[4] = o[3] + align256((size_t)2 * G * 4);
+    if (off)
+        for (int i = 0; i < 5; ++i) off[i] = o[i];
+    return o[4] + 256;
+}
+
+extern "C" size_t nvfp4b_ep_p2p_buffer_bytes(int G, int capacity, int H, size_t* offsets) {
+    if (G <= 0 || G > 256 || capacity <= 0 || H <= 0 || (H % 256)) return 0;
+    return p2p_layout(G, capacity, H, offsets);
+}
+
+extern "C" int nvfp4b_ep_p2p_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk,
+                                      int E, float in_gscale, const float* d_in_amax, void* workspace,
+                                      const nvfp4b_ep_peers* peers, int* overflow, void* stream) {
+    if (!x || !ids || !weights || !workspace || !overflow) return NVFP4B_ERR_NULL;
+    const int st = check_peers(peers);
+    if (st) return st;
+    const int G = peers->G;
+    if (T <= 0 || H <= 0 || (H % 256) || topk <= 0 || topk > 16 || E <= 0 || E > 256 || (E % G) || topk > E)
+        return NVFP4B_ERR_SHAPE;
+    if (!aligned16(x) || !aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    const Workspace w = carve(workspace, T, H, 32, E, topk);
+    return ep_dispatch_p2p(x, T, H, ids, weights, topk, E, in_gscale, d_in_amax, w, *peers, overflow,
+                           (cudaStream_t)stream);
+}
+
+extern "C" int nvfp4b_ep_p2p_expert_forward(const nvfp4b_moe_experts* ex, void* workspace,
+                                            const nvfp4b_ep_peers* peers, void* stream) {
+    if (!workspace) return NVFP4B_ERR_NULL;
+    int st = check_experts(ex);
+    if (st) return st;
+    st = check_peers(peers);
+    if (st) return st;
+    if (!aligned16(workspace)) return NVFP4B_ERR_ALIGN;
+    const int n = peers->G * peers->capacity;
+    const Workspace w = carve(workspace, n, ex->hidden, ex->inter, ex->num_experts, 1);
+    return ep_expert(peers->my_recv, peers->G, peers->capacity, peers->my_counts, ex, w, (cudaStream_t)stream,
+                     peers);
+}
+
+extern "C" int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace,
+                                     const nvfp4b_ep_peers* peers, float* out, int flags, void* stream) {
+    if (!workspace || !out) return NVFP4B_ERR_NULL;
+    const int st = check_peers(peers);
+    if (st) return st;
+    if (T <= 0 || H <= 0 || (H % 256) || topk <= 0 || topk > 16 || E <= 0) return NVFP4B_ERR_SHAPE;
+    if (flags & ~NVFP4B_MOE_ACCUMULATE) return NVFP4B_ERR_ARG;
+    if (!aligned16(out)) return NVFP4B_ERR_ALIGN;
+    int* err = device_error_ptr();
+    if (!err) return NVFP4B_ERR_CUDA;
+    const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
+    const long long threads = (long long)T * (H / 8);
+    ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        peers->my_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, peers->my_flags + peers->G,
+        peers->G, peers->state, err);
+    return launch_status();
+}
+
+extern "C" int nvfp4b_ep_p2p_state(const nvfp4b_ep_peers* peers, unsigned* host_words4) {
+    if (!peers || !peers->state || !host_words4) return NVFP4B_ERR_NULL;
+    const cudaError_t e = cudaMemcpy(host_words4, peers->state, 4 * sizeof(unsigned), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
+}
+
+extern "C" int nvfp4b_ep_p2p_recv_counts(const nvfp4b_ep_peers* peers, int* host_counts) {
+    if (!peers || !peers->my_counts || !host_counts) return NVFP4B_ERR_NULL;
+    if (peers->G <= 0 || peers->G > 256) return NVFP4B_ERR_SHAPE;
+    const cudaError_t e = cudaMemcpy(host_counts, peers->my_counts, peers->G * sizeof(int), cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
+}
+
+extern "C" int nvfp4b_ipc_alloc(size_t bytes, void** ptr) {
+    if (!ptr) return NVFP4B_ERR_NULL;
+    if (bytes == 0) return NVFP4B_ERR_SHAPE;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    e = cudaMemset(*ptr, 0, bytes);
+    if (e != cudaSuccess) return record_cuda_error(e);
+    return NVFP4B_OK;
+}
+
+extern "C" int nvfp4b_ipc_free(void* ptr) {
+    const cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
+}
+
+extern "C" int nvfp4b_ipc_handle(void* ptr, void* handle64) {
+    if (!ptr || !handle64) return NVFP4B_ERR_NULL;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+    const cudaError_t e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle64), ptr);
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
+}
+
+extern "C" int nvfp4b_ipc_open(const void* handle64, void** ptr) {
+    if (!handle64 || !ptr) return NVFP4B_ERR_NULL;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
+}
+
+extern "C" int nvfp4b_ipc_close(void* ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? NVFP4B_OK : record_cuda_error(e);
 }

@@ -26,6 +26,7 @@ enum DeviceError : int {
     kErrTimeoutProducer = 1,
     kErrTimeoutMma = 2,
     kErrTimeoutEpilogue = 3,
+    kErrTimeoutPeer = 4,          // an expert-parallel wait for another rank's flag expired
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

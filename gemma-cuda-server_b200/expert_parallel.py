@@ -12,6 +12,11 @@ sum).  This is the expert-parallel form of the same computation.  One layer, per
   5. all-to-all of the row slots back to their sources
   6. ops.combine: slot-ordered fp32 sum into out (bit-identical to the single-GPU layer at G = 1)
 
+P2PKernelOps runs the same layer with steps 3 and 5 fused into the kernels around them (nvfp4b_ep_p2p_*): the pack
+kernel stores records straight into the destination ranks' receive slots and the down-projection epilogue stores
+rows straight into the source ranks' return rows, over NVLink peer memory shared through CUDA IPC (PeerExchange);
+per-(rank pair, layer) flags replace the collectives, so forward() issues no collective at all.
+
 Every buffer has a fixed size, so nothing is read back to the host and a whole stack of layers can be captured in
 one CUDA graph.  A destination receiving more than `capacity` records from one source sets the overflow flag
 (check with overflowed() after the step); capacity = T_cap * topk never overflows.  `ops` does the device work;
@@ -69,6 +74,107 @@ class KernelOps:
         return self.pkg.ep_combine(back, self.T, self.topk, self.E, self.src_ws, out, accumulate=accumulate)
 
 
+class PeerExchange:
+    """One rank's exchange buffers (one zeroed device allocation: receive slots, return rows, counts, flags,
+    private state) and the device tables of every rank's buffers, as the nvfp4b_ep_peers the kernels take."""
+
+    def __init__(self, pkg, rank: int, G: int, capacity: int, H: int, base: int, bases: list[int],
+                 owned: list[int], opened: list[int], device="cuda"):
+        self.pkg, self.rank, self.G, self.capacity, self.H = pkg, rank, G, capacity, H
+        self.base, self._owned, self._opened = base, owned, opened
+        _, off = pkg.ep_p2p_buffer_layout(G, capacity, H)
+        self.off = off
+        self.tables = torch.tensor([[b + off[i] for b in bases] for i in range(4)], dtype=torch.int64, device=device)
+        tp = self.tables.data_ptr()
+        self.peers = pkg.EpPeers(rank, G, capacity, tp, tp + 8 * G, tp + 16 * G, tp + 24 * G,
+                                 base + off[0], base + off[1], base + off[2], base + off[3], base + off[4])
+
+    @classmethod
+    def local_group(cls, pkg, G: int, capacity: int, H: int, device="cuda") -> list["PeerExchange"]:
+        """G exchanges on the current device that address one another: emulated ranks for single-GPU tests.  Their
+        layers must run rank after rank on one stream (dispatch of every rank, then experts, then combines)."""
+        nbytes, _ = pkg.ep_p2p_buffer_layout(G, capacity, H)
+        bases = [pkg.ipc_alloc(nbytes) for _ in range(G)]
+        return [cls(pkg, r, G, capacity, H, bases[r], bases, [bases[r]], [], device) for r in range(G)]
+
+    @classmethod
+    def create(cls, pkg, G: int, capacity: int, H: int, group=None, device="cuda") -> "PeerExchange":
+        """This process's exchange in a group of G processes, one per GPU of the node: allocates, shares the CUDA
+        IPC handle with every rank (all_gather_object over `group`) and maps the others' buffers."""
+        rank = dist.get_rank(group)
+        nbytes, _ = pkg.ep_p2p_buffer_layout(G, capacity, H)
+        base = pkg.ipc_alloc(nbytes)
+        handles = [None] * G
+        dist.all_gather_object(handles, pkg.ipc_handle(base), group=group)
+        bases, opened = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                bases.append(base)
+            else:
+                p = pkg.ipc_open(h)
+                opened.append(p)
+                bases.append(p)
+        return cls(pkg, rank, G, capacity, H, base, bases, [base], opened, device)
+
+    def recv_counts(self) -> list[int]:
+        """Records this rank received from each source in the last layer (synchronous read)."""
+        return self.pkg.ep_p2p_recv_counts(self.peers)
+
+    def state_words(self) -> list[int]:
+        """This rank's private words [layer epoch, pack completions, down completions, spare] (synchronous)."""
+        return self.pkg.ep_p2p_state(self.peers)
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (call once every rank is done with them)."""
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self.pkg.ipc_close(p)
+        for p in self._owned:
+            self.pkg.ipc_free(p)
+        self._opened, self._owned = [], []
+
+
+class P2PKernelOps:
+    """Device side of one expert-parallel layer whose exchanges run over peer memory (no collective)."""
+
+    p2p = True
+
+    def __init__(self, pkg, experts, E: int, topk: int, T_cap: int, exchange: PeerExchange, device="cuda"):
+        G = exchange.G
+        if E % G:
+            raise ValueError(f"{E} experts do not split over {G} ranks")
+        if experts.E != E // G:
+            raise ValueError(f"local arena holds {experts.E} experts, expected {E // G}")
+        self.pkg, self.experts, self.E, self.topk, self.T_cap, self.G = pkg, experts, E, topk, T_cap, G
+        self.ex = exchange
+        self.capacity = exchange.capacity
+        self.H = experts.H
+        self.src_ws = pkg.moe_workspace(T_cap, experts.H, 32, E, topk, device=device)
+        self.exp_ws = pkg.moe_workspace(G * self.capacity, experts.H, experts.I, E // G, 1, device=device)
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
+
+    @staticmethod
+    def default_capacity(T_cap: int, topk: int, G: int) -> int:
+        """Even share n = T_cap * topk / G plus 8 sqrt(n) + 32, at most T_cap * topk (which cannot overflow)."""
+        share = T_cap * topk / G
+        return min(T_cap * topk, int(share + 8 * share ** 0.5 + 32 + 15) // 16 * 16)
+
+    def dispatch(self, x, ids, weights, in_gscale=None, in_amax=None):
+        T = x.shape[0]
+        if T > self.T_cap:
+            raise ValueError(f"{T} tokens exceed the capacity {self.T_cap}")
+        self.T = T
+        self.pkg.ep_p2p_dispatch(x, ids, weights, self.E, self.src_ws, self.ex.peers, self.overflow,
+                                 in_gscale=in_gscale, in_amax=in_amax)
+
+    def expert(self):
+        self.pkg.ep_p2p_expert_forward(self.experts, self.exp_ws, self.ex.peers)
+
+    def combine(self, out, accumulate: bool):
+        return self.pkg.ep_p2p_combine(self.T, self.topk, self.E, self.src_ws, self.ex.peers, out,
+                                       accumulate=accumulate)
+
+
 class ExpertParallelMoE:
     """Runs layers through `ops` over `group` (None = the default group; world size 1 runs with no collective)."""
 
@@ -82,6 +188,14 @@ class ExpertParallelMoE:
         """out[t] (+)= the layer's output for token t.  `mark(name)`, if given, is called around the expert-side
         kernels ("kernel" / "kernel_end") so a caller can time them with events on the current stream."""
         ops, G, grp = self.ops, self.G, self.group
+        if getattr(ops, "p2p", False):
+            ops.dispatch(x, ids, weights, in_gscale=in_gscale, in_amax=in_amax)
+            if mark is not None:
+                mark("kernel")
+            ops.expert()
+            if mark is not None:
+                mark("kernel_end")
+            return ops.combine(out, accumulate)
         send_counts, recv_counts = ops.dispatch(x, ids, weights, in_gscale=in_gscale, in_amax=in_amax)
         if G > 1:
             dist.all_to_all_single(recv_counts, send_counts, group=grp)

@@ -279,6 +279,70 @@ int nvfp4b_ep_expert_forward(const uint8_t* records, int G, int capacity, const 
 int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk, int E, const void* workspace, float* out,
                       int flags, void* stream);
 
+/* ---- Expert parallelism over NVLink peer memory (one process per GPU, no collective library on the data path) --
+ *
+ * The same layer with the two all-to-alls fused into the kernels around them: the source rank's pack kernel stores
+ * each record straight into the destination rank's receive slots (its block `rank`), and the expert rank's down-
+ * projection epilogue stores each weighted fp16 row straight into the source rank's return rows (block `rank`),
+ * both with plain stores to peer memory over NVLink.  Only the records that exist cross the link.  Completion is
+ * published per (rank pair, layer) with a release store of the layer's epoch to a flag word in the receiver's
+ * memory, written by the last block of the producing kernel after a system-scope fence; the receiving kernels
+ * (record scatter, combine) acquire it with a bounded spin (NVFP4B_ERR_TIMEOUT in the device error word after
+ * ~10 s; the kernel then goes on and the context stays usable).  Layer order per rank, all on one stream:
+ *   nvfp4b_ep_p2p_dispatch -> nvfp4b_ep_p2p_expert_forward -> nvfp4b_ep_p2p_combine
+ * Results are bit-identical to nvfp4b_moe_forward over all experts (same quantisation, same slot-ordered sum).
+ * Exchange buffers live in one device allocation per rank (nvfp4b_ipc_alloc), shared with the other ranks through
+ * CUDA IPC handles; every pointer below is a device pointer in the calling rank's address space. */
+typedef struct nvfp4b_ep_peers {
+    int rank, G, capacity;        /* this rank, ranks, record slots per (source, destination) pair */
+    uint8_t* const* recv;         /* device array [G]: rank g's receive slots [G * capacity] records */
+    uint16_t* const* back;        /* device array [G]: rank g's return rows [G * capacity, H] fp16 */
+    int* const* counts;           /* device array [G]: rank g's receive counts [G] int32 */
+    unsigned* const* flags;       /* device array [G]: rank g's flag words [2G] (records landed / rows landed) */
+    uint8_t* my_recv;             /* this rank's own buffers: entries `rank` of the arrays above */
+    uint16_t* my_back;
+    int* my_counts;
+    unsigned* my_flags;
+    unsigned* state;              /* this rank's 4 private words (layer epoch, completion counters) */
+} nvfp4b_ep_peers;
+
+/* Bytes of one rank's exchange buffers and their offsets inside it (each 256-byte aligned): receive slots, return
+ * rows, counts, flags, state.  offsets[5] may be NULL.  The flags, counts and state must be zero before the first
+ * layer (nvfp4b_ipc_alloc zeroes the whole allocation). */
+size_t nvfp4b_ep_p2p_buffer_bytes(int G, int capacity, int H, size_t* offsets);
+
+/* Source side: as nvfp4b_ep_dispatch, records stored into the destinations' receive slots and counts, then the
+ * records-landed flags raised and this rank's layer epoch advanced.  *overflow |= 1 if a destination would get
+ * more than capacity records (excess not sent).  workspace: nvfp4b_moe_workspace_bytes(T, H, 32, E, topk), kept
+ * until nvfp4b_ep_p2p_combine. */
+int nvfp4b_ep_p2p_dispatch(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E,
+                           float in_gscale, const float* d_in_amax, void* workspace, const nvfp4b_ep_peers* peers,
+                           int* overflow, void* stream);
+
+/* Expert side: waits for every source's records of this layer, runs the local experts (experts->num_experts =
+ * E / G) and stores the weighted rows into the sources' return rows, then raises the rows-landed flags.
+ * workspace: nvfp4b_moe_workspace_bytes(G * capacity, H, I, E / G, 1). */
+int nvfp4b_ep_p2p_expert_forward(const nvfp4b_moe_experts* experts, void* workspace, const nvfp4b_ep_peers* peers,
+                                 void* stream);
+
+/* Source side: waits for every expert rank's rows of this layer and sums them into out in slot order (flags:
+ * NVFP4B_MOE_ACCUMULATE or 0).  `workspace` is the one given to nvfp4b_ep_p2p_dispatch. */
+int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
+                          float* out, int flags, void* stream);
+
+/* Debug reads (synchronous, not for capture): a rank's private words (layer epoch, completion counters, spare) and
+ * its receive counts [G] (records from each source in the last layer). */
+int nvfp4b_ep_p2p_state(const nvfp4b_ep_peers* peers, unsigned* host_words4);
+int nvfp4b_ep_p2p_recv_counts(const nvfp4b_ep_peers* peers, int* host_counts);
+
+/* Set-up helpers (not capture-safe, they allocate or map): a zeroed device allocation whose CUDA IPC handle
+ * (64 bytes) another process on the node maps with nvfp4b_ipc_open (peer access enabled lazily). */
+int nvfp4b_ipc_alloc(size_t bytes, void** ptr);
+int nvfp4b_ipc_free(void* ptr);
+int nvfp4b_ipc_handle(void* ptr, void* handle64);
+int nvfp4b_ipc_open(const void* handle64, void** ptr);
+int nvfp4b_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

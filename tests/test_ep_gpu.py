@@ -91,3 +91,66 @@ def test_ep_overflow_is_flagged():
     ops, *_ = _emulate(p, P, G, T, capacity=16)          # ~T*8/2 = 256 records per pair on average
     assert all(int(o.overflow.item()) == 1 for o in ops)
     assert all(int(c) <= 16 for o in ops for c in o.counts.tolist())
+
+
+# ---- exchange over peer memory (nvfp4b_ep_p2p_*): records and rows stored into the other ranks' buffers ----------
+
+def _emulate_p2p(p, P, G, T, capacity=None, layers=1):
+    """G ranks on one GPU sharing exchange buffers: every rank's dispatch, then every rank's experts, then every
+    rank's combine, on one stream (each wait finds its flags already raised).  `layers` repeats the layer to check
+    that the per-layer epochs advance."""
+    import gemma_cuda_server_b200.expert_parallel as epm
+    E, k, H = P["E"], P["topk"], P["H"]
+    C = capacity or epm.P2PKernelOps.default_capacity(T, k, G)
+    ex = epm.PeerExchange.local_group(p, G, C, H)
+    ops = [epm.P2PKernelOps(p, P["arena"].slice(r * E // G, (r + 1) * E // G), E, k, T, ex[r]) for r in range(G)]
+    xs = [P["x"][r * T:(r + 1) * T].contiguous() for r in range(G)]
+    ids = [P["ids"][r * T:(r + 1) * T].contiguous() for r in range(G)]
+    ws = [P["w"][r * T:(r + 1) * T].contiguous() for r in range(G)]
+    amaxes = [p.amax(x) for x in xs]
+    outs = [torch.full((T, H), float("nan"), device="cuda") for _ in range(G)]
+    for _ in range(layers):
+        for r in range(G):
+            ops[r].dispatch(xs[r], ids[r], ws[r], in_amax=amaxes[r])
+        for r in range(G):
+            ops[r].expert()
+        for r in range(G):
+            ops[r].combine(outs[r], False)
+    torch.cuda.synchronize()
+    return ex, ops, xs, ids, ws, amaxes, outs
+
+
+@pytest.mark.parametrize("G,layers", [(1, 1), (2, 3), (4, 2)])
+def test_ep_p2p_emulated_ranks_bit_identical(G, layers):
+    T = 96
+    p, P = make_problem(T * G, 512, 128, 32, 8, seed=53)
+    P["ids"], P["w"], _, _ = route_and_calibrate(p, P)
+    ex, ops, xs, ids, ws, amaxes, outs = _emulate_p2p(p, P, G, T, layers=layers)
+    try:
+        assert p.read_device_error() == 0
+        assert not any(int(o.overflow.item()) for o in ops)
+        for r in range(G):
+            ref = _ref(p, P, xs[r], ids[r], ws[r], amaxes[r])
+            torch.cuda.synchronize()
+            assert torch.equal(outs[r], ref), f"rank {r}: max diff {(outs[r] - ref).abs().max().item()}"
+        for e in ex:                                   # epoch = layers run; completion counters back at zero
+            assert e.state_words()[:3] == [layers, 0, 0]
+        total = sum(sum(e.recv_counts()) for e in ex)
+        assert total == G * T * P["topk"]              # every assignment crossed exactly once
+    finally:
+        for e in ex:
+            e.close()
+
+
+def test_ep_p2p_overflow_is_flagged():
+    G, T = 2, 64
+    p, P = make_problem(T * G, 512, 128, 32, 8, seed=59)
+    P["ids"], P["w"], _, _ = route_and_calibrate(p, P)
+    ex, ops, *_ = _emulate_p2p(p, P, G, T, capacity=16)
+    try:
+        assert p.read_device_error() == 0
+        assert all(int(o.overflow.item()) == 1 for o in ops)
+        assert all(c <= 16 for e in ex for c in e.recv_counts())
+    finally:
+        for e in ex:
+            e.close()
