@@ -411,19 +411,21 @@ __device__ __forceinline__ bool last_block_arrived(unsigned* counter) {
 }
 
 // Thread 0 of a block: waits until flags[g] >= epoch for every g < G (acquire, system scope; bounded, a timeout is
-// recorded in *err and the wait ends); the block barrier then makes what the flags publish visible to the block.
+// recorded in *err and the wait ends, and once *err is set no later wait spins at all); the block barrier then
+// makes what the flags publish visible to the block.
 __device__ __forceinline__ void wait_peer_flags(const unsigned* flags, int G, unsigned epoch, int* err) {
     if (threadIdx.x == 0) {
         bool ok = true;
+        const volatile int* verr = err;
         for (int g = 0; g < G && ok; ++g) {
             if ((int)(ld_acquire_sys(flags + g) - epoch) >= 0) continue;
             const unsigned long long t0 = sm100::globaltimer();
             while ((int)(ld_acquire_sys(flags + g) - epoch) < 0) {
-                if (sm100::globaltimer() - t0 > kPeerWaitNs) { ok = false; break; }
+                if (*verr != 0 || sm100::globaltimer() - t0 > kPeerWaitNs) { ok = false; break; }
                 __nanosleep(64);
             }
         }
-        if (!ok) atomicCAS(err, 0, sm100::kErrTimeoutPeer);
+        if (!ok) atomicCAS(err, 0, sm100::kErrTimeoutPeer);   // keeps an error recorded earlier
     }
     __syncthreads();
 }

@@ -79,7 +79,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_ep_p2p_processes_bit_identical(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
