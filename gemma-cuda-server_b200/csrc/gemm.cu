@@ -113,6 +113,7 @@ struct DenseEpi {
     }
 
     __device__ __forceinline__ void finish() const {}
+    __device__ __forceinline__ bool row_live(const TileInfo&, int) const { return true; }
 
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],

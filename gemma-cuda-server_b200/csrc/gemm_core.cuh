@@ -368,14 +368,16 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             tc_fence_after();
             const uint32_t addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(abuf * C::BN + col_base);
             uint32_t r[C::CHUNKS][32];
-            if (col_base < ti.n_mma) {
+            // a warp whose 32 rows the epilogue policy marks dead (padding) neither loads nor processes them
+            const bool work = col_base < ti.n_mma && __any_sync(0xFFFFFFFFu, epi.row_live(ti, row));
+            if (work) {
 #pragma unroll
                 for (int c = 0; c < C::CHUNKS; ++c) tmem_ld_32x32b_x32(addr + 32 * c, r[c]);
                 tmem_wait_ld();
             }
             tc_fence_before();
             mbar_arrive(&tempty[abuf]);          // accumulator drained: the next tile's MMAs may start
-            if (col_base < ti.n_mma) epi.template process<C::CHUNKS>(ti, row, col_base, r, esm);
+            if (work) epi.template process<C::CHUNKS>(ti, row, col_base, r, esm);
             if (++abuf == C::ACC_BUFS) { abuf = 0; aphase ^= 1u; }
         }
         epi.finish();

@@ -113,6 +113,7 @@ struct RouterEpi {
     long long split_stride;  // T * E
     int T, E;
     __device__ __forceinline__ void finish() const {}
+    __device__ __forceinline__ bool row_live(const TileInfo&, int) const { return true; }
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
                                             uint8_t*) const {
@@ -454,6 +455,10 @@ struct GateUpEpi {
     const int* row_token;
 
     __device__ __forceinline__ void finish() const {}
+    // Rows of expert-segment padding hold no token: a warp whose 32 rows are all padding skips its work.
+    __device__ __forceinline__ bool row_live(const TileInfo& ti, int row) const {
+        return __ldg(row_token + (long long)ti.a_row + row) >= 0;
+    }
 
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
@@ -548,6 +553,12 @@ struct DownEpi {
     unsigned* state = nullptr;
     int rank = 0, G = 0, capacity = 0;
 
+    // Padding rows of an expert segment (row_assign -1) produce nothing: a warp whose 32 rows are all padding skips
+    // its work.
+    __device__ __forceinline__ bool row_live(const TileInfo& ti, int row) const {
+        return __ldg(row_assign + (long long)ti.a_row + row) >= 0;
+    }
+
     // Every epilogue warp (warps 4.. of every CTA) calls this once after its last tile.
     __device__ __forceinline__ void finish() const {
         if constexpr (DETERMINISTIC) {
@@ -566,40 +577,32 @@ struct DownEpi {
         }
     }
 
-    // DETERMINISTIC: each warp transposes its 32-row x 32-column chunk through shared memory (32 x 33 floats) so
-    // every store instruction writes four full 64-byte row segments of y instead of 32 scattered 8-byte pieces.
+    // DETERMINISTIC: each lane converts its row's 32-column chunk to fp16 and stores it as four 16-byte pieces (64
+    // contiguous bytes of the row); no shared-memory transpose, so the epilogue's per-tile cost -- which bounds this
+    // short-K GEMM -- is a handful of instructions per chunk.
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
-                                            uint8_t* esm) const {
+                                            uint8_t*) const {
         const long long m = (long long)ti.a_row + row;
         const int a = __ldg(row_assign + m);
         const int e = ti.expert;
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
-            const int lane = threadIdx.x & 31;
-            uint16_t* rowp = nullptr;
-            if (a >= 0)
-                rowp = peer_back ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
-                                 : y + (long long)a * H;
-            float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 4) * (32 * 33);   // epilogue warps are 4..
-            const int sub = lane >> 3, q = (lane & 7) * 4;
+            if (a < 0) return;
+            uint16_t* rowp = peer_back ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
+                                       : y + (long long)a * H;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
-                const int n0 = ti.n0 + col_base + 32 * c;   // warp-uniform
+                const int n0 = ti.n0 + col_base + 32 * c;
                 if (n0 >= H) continue;
-                __syncwarp();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = s * __uint_as_float(r[c][i]);
-                __syncwarp();
-#pragma unroll
-                for (int g = 0; g < 8; ++g) {
-                    const int i = 4 * g + sub;
-                    uint16_t* pi = reinterpret_cast<uint16_t*>(
-                        __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), i));
-                    const float* src = tile + i * 33 + q;
-                    if (pi)
-                        *reinterpret_cast<uint2*>(pi + n0 + q) =
-                            make_uint2(pack_half2_sat(src[0], src[1]), pack_half2_sat(src[2], src[3]));
+                for (int q = 0; q < 4; ++q) {
+                    uint4 v;
+                    v.x = pack_half2_sat(s * __uint_as_float(r[c][8 * q + 0]), s * __uint_as_float(r[c][8 * q + 1]));
+                    v.y = pack_half2_sat(s * __uint_as_float(r[c][8 * q + 2]), s * __uint_as_float(r[c][8 * q + 3]));
+                    v.z = pack_half2_sat(s * __uint_as_float(r[c][8 * q + 4]), s * __uint_as_float(r[c][8 * q + 5]));
+                    v.w = pack_half2_sat(s * __uint_as_float(r[c][8 * q + 6]), s * __uint_as_float(r[c][8 * q + 7]));
+                    *reinterpret_cast<uint4*>(rowp + n0 + 8 * q) = v;
                 }
             }
         } else {
@@ -851,7 +854,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back,
 }
 
 using GroupCfg = KCfg<256, 4, 1, 8>;
-using DownCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // K = I is short: 3 stages + transpose tiles
+using DownCfg = KCfg<256, 4, 1, 8>;   // K = I is short: the epilogue bounds it (direct fp16 row stores)
 
 // ---------------------------------------------------------------------------------------------------------------
 // host orchestration
