@@ -58,9 +58,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep"], default="ep")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--ep-exchange", choices=["auto", "p2p", "nccl"], default="auto",
+    ap.add_argument("--ep-exchange", choices=["auto", "p2p", "nccl", "local"], default="auto",
                     help="ep: records/rows stored over NVLink peer memory by the kernels (p2p), NCCL all-to-all "
-                         "(nccl), or auto = p2p on 2+ GPUs and the local path (no exchange at all) on 1")
+                         "(nccl), the single-GPU MoE layer (local, 1 GPU only), or auto = p2p on 2+ GPUs, local on 1")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
     return ap.parse_args()
@@ -429,6 +429,7 @@ class EpWorkload:
             del w2
             arena.w2_gscale.fill_(g2)
             ops = (epm.P2PKernelOps(pkg, arena, E, topk, T, self.ex) if exchange == "p2p"
+                   else epm.LocalOps(pkg, arena, E, topk, T) if exchange == "local"
                    else epm.KernelOps(pkg, arena, E, topk, T_cap=T, G=world))
             Ld = dict(proj=proj, arena=arena, ops=ops, layer=epm.ExpertParallelMoE(ops, group),
                       amax=torch.zeros(1, device="cuda"), ids=torch.empty((T, topk), dtype=torch.int32, device="cuda"),
@@ -448,14 +449,16 @@ class EpWorkload:
         torch.cuda.synchronize()
         del cal_ws
         self.units_per_step = T                                   # rows of this rank; value() scales by G
-        self.launches_per_step = 16 * L   # per layer: amax, router x2, dispatch x4, expert x8, combine
+        # per layer: amax, router x2, then dispatch x4, expert x8, combine (exchange paths) or the single-GPU layer's
+        # hist/plan/rank/pad/quant-scatter, gate/up, down, combine (local)
+        self.launches_per_step = (11 if exchange == "local" else 16) * L
         self.kernel_flops = 2.0 * T * topk * 3 * I * H            # expert GEMMs of one layer at even routing
         self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
         self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_per_gpu": T, "hidden": H,
                        "experts": E, "experts_per_gpu": El, "inter": I, "topk": topk,
                        "exchange": ("NVFP4 records and fp16 rows stored to peer memory over NVLink by the pack kernel "
                                     "and the down-GEMM epilogue, per-layer flags (no collective)") if exchange == "p2p"
-                       else ("none (one GPU holds every expert)" if world == 1
+                       else ("none: one GPU holds every expert (single-GPU MoE layer)" if exchange == "local"
                              else "NCCL all-to-all of NVFP4 records and fp16 rows per layer"),
                        "l2": "flushed between steps (256 MiB write + 256 MiB read)", "step_flops": self.step_flops}
 
@@ -492,6 +495,8 @@ class EpWorkload:
         """Records this rank's experts ran in layer li's last run."""
         if self.exchange == "p2p":
             return sum(self.ex.recv_counts())        # one exchange for all layers: the last layer's counts
+        if self.exchange == "local":
+            return self.T * self.topk
         return int(self.layers[li]["ops"].counts[self.G:].sum().item())
 
     def close(self):
@@ -643,7 +648,9 @@ def main():
     pkg = load_package()
     pkg.lib()
     if args.workload == "ep":
-        exchange = args.ep_exchange if args.ep_exchange != "auto" else ("p2p" if world > 1 else "nccl")
+        exchange = args.ep_exchange if args.ep_exchange != "auto" else ("p2p" if world > 1 else "local")
+        if exchange == "local" and world > 1:
+            raise SystemExit("--ep-exchange local needs one GPU")
         W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange)
     else:
         W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload}[args.workload](pkg, torch, orc)
@@ -775,7 +782,9 @@ def main():
         fp4_peak = peaks["bf16_tflops"] * 4.0
         roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
                 "frac": achieved / fp4_peak, "traffic": None,
-                "kernel": "expert side of one layer (record scatter, grouped gate/up and down GEMMs)",
+                "kernel": ("one MoE layer (dispatch with fused quantiser, grouped gate/up and down GEMMs, combine)"
+                           if W.exchange == "local" else
+                           "expert side of one layer (record scatter, grouped gate/up and down GEMMs)"),
                 "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
                 "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
     else:

@@ -332,19 +332,25 @@ __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ se
 // 3. quantise once, scatter to every destination row
 // ---------------------------------------------------------------------------------------------------------------
 
+constexpr int kScatterWarps = 4;   // warps per token in the quantise-and-scatter kernels
+
+// kScatterWarps warps per token: warp `part` quantises every kScatterWarps-th run of 32 blocks of x[t] once and
+// writes each block to all of the token's destination rows.
 __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* __restrict__ x, int T, int H,
                                                                 int topk, const int* __restrict__ dest,
                                                                 float gscale, const float* __restrict__ d_amax,
                                                                 uint8_t* __restrict__ a_codes,
                                                                 uint8_t* __restrict__ a_scales, int tile_cols) {
     const int lane = threadIdx.x & 31;
-    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    const int t = gw / kScatterWarps, part = gw % kScatterWarps;
     if (t >= T) return;
     const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
     const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
     const int kb = H >> 4;
     const uint16_t* xr = x + (long long)t * H;
-    for (int b = lane; b - lane < kb; b += 32) {
+    for (int b0 = part * 32; b0 < kb; b0 += 32 * kScatterWarps) {
+        const int b = b0 + lane;
         uint32_t w0 = 0, w1 = 0, sf = 0;
         if (b < kb) {
             const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
@@ -622,33 +628,32 @@ struct DownEpi {
     }
 };
 
-// out[t] (+)= sum_j y[t*k + j] over the k slots in order, fp32 accumulation of the fp16 rows.  One warp per token,
-// 8 columns (16 bytes of y) per lane step; H % 256 == 0.
+// out[t] (+)= sum_j y[t*k + j] over the k slots in order, fp32 accumulation of the fp16 rows.  One thread per
+// (token, 8 columns): T * H / 8 independent 16-byte gathers; H % 8 == 0.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const uint16_t* __restrict__ y, int T, int H, int topk,
                                                           float* __restrict__ out, int accumulate) {
-    const int lane = threadIdx.x & 31;
-    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (t >= T) return;
-    const uint16_t* src = y + (long long)t * topk * H;
-    float* dst = out + (long long)t * H;
-    for (int c = lane * 8; c < H; c += 256) {
-        float acc[8];
-        if (accumulate) {
-            const float4 u = *reinterpret_cast<const float4*>(dst + c), v = *reinterpret_cast<const float4*>(dst + c + 4);
-            acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
-        } else {
+    const int chunks = H >> 3;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)T * chunks) return;
+    const int t = (int)(idx / chunks), c = (int)(idx - (long long)t * chunks) * 8;
+    const uint16_t* src = y + (long long)t * topk * H + c;
+    float* dst = out + (long long)t * H + c;
+    float acc[8];
+    if (accumulate) {
+        const float4 u = *reinterpret_cast<const float4*>(dst), v = *reinterpret_cast<const float4*>(dst + 4);
+        acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
+    } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        }
-        for (int j = 0; j < topk; ++j) {
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + (long long)j * H + c));
-            const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
-            acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
-            acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
-        }
-        *reinterpret_cast<float4*>(dst + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        *reinterpret_cast<float4*>(dst + c + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     }
+    for (int j = 0; j < topk; ++j) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + (long long)j * H));
+        const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
+        acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+        acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+    }
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -884,7 +889,7 @@ int dispatch(const void* x, int T, const int* ids, const float* weights, int top
     const int tile_cols = (H / 16 + 3) / 4;
     moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
                                      w.row_weight, w.row_assign, nullptr);
-    moe_quant_scatter_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
+    moe_quant_scatter_kernel<<<(T * kScatterWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
                                                          in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols);
     return launch_status();
 }
@@ -968,7 +973,8 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
         }
         st = launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
         if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
-        moe_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(w.y, T, H, topk, out, accumulate ? 1 : 0);
+        moe_combine_kernel<<<(unsigned)(((long long)T * (H / 8) + 255) / 256), 256, 0, s>>>(w.y, T, H, topk, out,
+                                                                                      accumulate ? 1 : 0);
         return launch_status();
     }
     if (!accumulate) {

@@ -175,6 +175,28 @@ class P2PKernelOps:
                                        accumulate=accumulate)
 
 
+class LocalOps:
+    """One GPU holding every expert: the layer is the single-GPU MoE (nvfp4b_moe_forward: dispatch with the
+    quantiser fused in, grouped GEMMs, slot-ordered combine) -- no records and no exchange.  Same result, bit for
+    bit, as the expert-parallel paths at G = 1."""
+
+    local = True
+
+    def __init__(self, pkg, experts, E: int, topk: int, T_cap: int, device="cuda"):
+        if experts.E != E:
+            raise ValueError(f"local arena holds {experts.E} experts, expected {E}")
+        self.pkg, self.experts, self.E, self.topk, self.T_cap, self.G = pkg, experts, E, topk, T_cap, 1
+        self.H = experts.H
+        self.src_ws = pkg.moe_workspace(T_cap, experts.H, experts.I, E, topk, device=device)
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def layer(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False):
+        if x.shape[0] > self.T_cap:
+            raise ValueError(f"{x.shape[0]} tokens exceed the capacity {self.T_cap}")
+        return self.pkg.moe_forward(x, ids, weights, self.experts, self.src_ws, in_gscale=in_gscale, in_amax=in_amax,
+                                    out=out, accumulate=accumulate)
+
+
 class ExpertParallelMoE:
     """Runs layers through `ops` over `group` (None = the default group; world size 1 runs with no collective)."""
 
@@ -188,6 +210,13 @@ class ExpertParallelMoE:
         """out[t] (+)= the layer's output for token t.  `mark(name)`, if given, is called around the expert-side
         kernels ("kernel" / "kernel_end") so a caller can time them with events on the current stream."""
         ops, G, grp = self.ops, self.G, self.group
+        if getattr(ops, "local", False):
+            if mark is not None:
+                mark("kernel")
+            ops.layer(x, ids, weights, out, in_gscale=in_gscale, in_amax=in_amax, accumulate=accumulate)
+            if mark is not None:
+                mark("kernel_end")
+            return out
         if getattr(ops, "p2p", False):
             ops.dispatch(x, ids, weights, in_gscale=in_gscale, in_amax=in_amax)
             if mark is not None:
