@@ -37,7 +37,15 @@
 namespace nvfp4b {
 namespace {
 
-constexpr int kRouterSplits = 4;
+constexpr int kRouterMaxSplits = 16;
+
+// Most split-K slices the router GEMM may use for T tokens x E experts: 16, or fewer so the fp32 partials stay
+// within 4 MiB (at least 4).  The workspace holds this many [T, E] partial slices.
+inline int router_max_splits(int T, int E) {
+    const long long te = (long long)T * E;
+    const long long fit = te > 0 ? (1ll << 20) / te : kRouterMaxSplits;
+    return (int)(fit < 4 ? 4 : fit > kRouterMaxSplits ? kRouterMaxSplits : fit);
+}
 constexpr int kChunk = 256;           // assignments per histogram / rank chunk (one rank round per CTA)
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -80,7 +88,7 @@ Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     char* p = static_cast<char*>(base);
     size_t off = 0;
     auto take = [&](size_t bytes) { char* q = p ? p + off : nullptr; off += align256(bytes); return q; };
-    w.partial = (float*)take((size_t)kRouterSplits * T * E * 4);
+    w.partial = (float*)take((size_t)router_max_splits(T, E) * T * E * 4);
     w.hist = (int*)take((size_t)n_chunks * E * 4);
     w.chunk_base = (int*)take((size_t)n_chunks * E * 4);
     w.seg_start = (int*)take((size_t)E * 4);
@@ -144,13 +152,22 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
     const int lane = threadIdx.x & 31;
     const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     if (t >= T) return;
+    // Sum of the split-K partial logits in split order; four splits' loads are issued together.
     float l[EPL];
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-        const int e = lane + 32 * i;
-        float acc = 0.f;
-        for (int s = 0; s < splits; ++s) acc += __ldg(partial + s * split_stride + (long long)t * E + e);
-        l[i] = acc;
+    for (int i = 0; i < EPL; ++i) l[i] = 0.f;
+    const float* pt = partial + (long long)t * E + lane;
+    for (int s0 = 0; s0 < splits; s0 += 4) {
+        float v[4][EPL];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) v[u][i] = s0 + u < splits ? __ldg(pt + (s0 + u) * split_stride + 32 * i) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < EPL; ++i)
+                if (s0 + u < splits) l[i] += v[u][i];
     }
     if (xnorm) {   // reference k_router_hn: x * rsqrt(mean(x^2) + 1e-6) * H^-0.5 (scale folded into proj)
         const uint16_t* xr = xnorm + (long long)t * H;
@@ -332,7 +349,7 @@ __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ se
 // 3. quantise once, scatter to every destination row
 // ---------------------------------------------------------------------------------------------------------------
 
-constexpr int kScatterWarps = 4;   // warps per token in the quantise-and-scatter kernels
+constexpr int kScatterWarps = 6;   // warps per token in the quantise-and-scatter kernel (6 x 32 lanes >= H/16 = 176)
 
 // kScatterWarps warps per token: warp `part` quantises every kScatterWarps-th run of 32 blocks of x[t] once and
 // writes each block to all of the token's destination rows.
@@ -713,7 +730,7 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hi
 // (dest = compact expert-sorted position), or -1 past the capacity (overflowed, not sent).  The record goes to
 // records[slot], or with peers.recv to peer d's receive slot rank * capacity + (slot - d * capacity); the last
 // block then stores the per-destination counts, raises the records-landed flags and advances the layer epoch.
-constexpr int kPackWarps = 4;
+constexpr int kPackWarps = 6;
 
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
                                                       const int* __restrict__ dest, const int* __restrict__ ids,
@@ -1136,12 +1153,16 @@ static int route_launch(const void* x, int T, int H, const void* proj, int E, in
     cp.sfb = nullptr;
     cp.tile_cols = (H * 2) / 32;
     cp.k_tiles = (cp.tile_cols + 3) / 4;
-    // Every split must own at least one K tile: an empty split would store an accumulator no MMA wrote.
-    const int kt_per_split = (cp.k_tiles + kRouterSplits - 1) / kRouterSplits;
-    const int splits = (cp.k_tiles + kt_per_split - 1) / kt_per_split;
     SplitKSched<RouterCfg::BN> sc{};
     sc.m_tiles = (T + 127) / 128;
     sc.n_tiles = (E + RouterCfg::BN - 1) / RouterCfg::BN;
+    // Enough K splits for about one tile per SM (small T has few row blocks), within router_max_splits.  Every split
+    // must own at least one K tile: an empty split would store an accumulator no MMA wrote.
+    const int per_split = sc.m_tiles * sc.n_tiles;
+    int want = (sm_count() + per_split - 1) / per_split;
+    want = want < 1 ? 1 : want > router_max_splits(T, E) ? router_max_splits(T, E) : want;
+    const int kt_per_split = (cp.k_tiles + want - 1) / want;
+    const int splits = (cp.k_tiles + kt_per_split - 1) / kt_per_split;
     sc.splits = splits;
     sc.kt_per_split = kt_per_split;
     sc.k_tiles = cp.k_tiles;
@@ -1203,8 +1224,9 @@ extern "C" int nvfp4b_moe_route(const void* x, int T, int H, const void* proj, i
 // workspace arena to pass to nvfp4b_moe_route.  This entry keeps the split-K partial logits in a file-scope device
 // array instead, so the call allocates nothing (no cudaMalloc/cudaFree, no library allocator).
 //
-// Limit: kRouteScratchBytes (4 MiB) of partials, i.e. kRouterSplits * T * E * 4 bytes: T * E <= 262144 (T <= 2048 at
-// E = 128).  Larger calls are rejected with NVFP4B_ERR_SCRATCH before anything is launched.
+// Limit: kRouteScratchBytes (4 MiB) of partials, i.e. router_max_splits(T, E) * T * E * 4 bytes, which holds exactly
+// when T * E <= 262144 (T <= 2048 at E = 128).  Larger calls are rejected with NVFP4B_ERR_SCRATCH before anything is
+// launched.
 // The array is one per device and per loaded library: calls that overlap in time on the same device (two streams,
 // or two host threads without ordering between their streams) race on it and produce wrong routes.
 constexpr size_t kRouteScratchBytes = size_t(4) << 20;
@@ -1236,7 +1258,8 @@ extern "C" int nvfp4b_moe_route_noalloc(const void* x, int T, int H, const void*
                                         void* stream) {
     const int st = route_checks(x, T, H, proj, E, topk, ids, weights);
     if (st) return st;
-    if ((size_t)kRouterSplits * (size_t)T * (size_t)E * sizeof(float) > kRouteScratchBytes) return NVFP4B_ERR_SCRATCH;
+    if ((size_t)router_max_splits(T, E) * (size_t)T * (size_t)E * sizeof(float) > kRouteScratchBytes)
+        return NVFP4B_ERR_SCRATCH;
     float* partial = route_scratch_ptr();
     if (!partial) return NVFP4B_ERR_CUDA;
     return route_launch(x, T, H, proj, E, topk, per_expert_scale, norm, ids, weights, partial, (cudaStream_t)stream);
