@@ -107,8 +107,9 @@ def test_router_matches_oracle(norm, T, H, E):
         assert np.allclose(got_w.sum(1), 1.0, atol=1e-5)      # renormalised top-k weights
 
 
-def test_dispatch_plan_and_dispatched_rows_bit_exact():
-    p, P = make_problem(300, 512, 128, 32, 8, seed=11)
+@pytest.mark.parametrize("T", [300, 1100])
+def test_dispatch_plan_and_dispatched_rows_bit_exact(T):
+    p, P = make_problem(T, 512, 128, 32, 8, seed=11)
     ids, w, _, _ = route_and_calibrate(p, P)
     out = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_gscale=float(P["g_in"]))
     torch.cuda.synchronize()
