@@ -408,6 +408,7 @@ class EpWorkload:
         self.x0 = torch.randn((T, H), generator=gen, device="cuda").to(torch.bfloat16)
         self.x = torch.empty_like(self.x0)
         self.res = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        self.amax = torch.zeros(1, dtype=torch.float32, device="cuda")
         cal_ws = pkg.moe_workspace(T, H, I, El, topk)
         self.layers = []
         x = self.x0.clone()
@@ -449,9 +450,10 @@ class EpWorkload:
         torch.cuda.synchronize()
         del cal_ws
         self.units_per_step = T                                   # rows of this rank; value() scales by G
-        # per layer: amax, router x2, then dispatch x4, expert x8, combine (exchange paths) or the single-GPU layer's
-        # hist/plan/rank/pad/quant-scatter, gate/up, down, combine (local)
-        self.launches_per_step = (11 if exchange == "local" else 16) * L
+        # one amax, then per layer: router x2 + dispatch x4, expert x8, combine with the next input fused (p2p); the
+        # single-GPU layer's hist/plan/rank/pad/quant-scatter, gate/up, down, combine (local); + the amax of the
+        # next input (nccl, where the combine has no fused output)
+        self.launches_per_step = {"local": 10, "p2p": 15, "nccl": 16}[exchange] * L + 1
         self.kernel_flops = 2.0 * T * topk * 3 * I * H            # expert GEMMs of one layer at even routing
         self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
         self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_per_gpu": T, "hidden": H,
@@ -466,12 +468,12 @@ class EpWorkload:
         p, k = self.pkg, self.topk
         self.x.copy_(self.x0)
         self.res.copy_(self.x0)
+        p.amax(self.x, out=self.amax)
         for li, Ld in enumerate(self.layers):
-            p.amax(self.x, out=Ld["amax"])
             p.moe_route(self.x, Ld["proj"], k, Ld["ops"].src_ws, ids=Ld["ids"], weights=Ld["w"])
-            Ld["layer"].forward(self.x, Ld["ids"], Ld["w"], self.res, in_amax=Ld["amax"], accumulate=True,
-                                mark=mark if li == 0 else None)
-            self.x.copy_(self.res)
+            # residual stream: res += MoE(x); the combine also leaves x = bf16(res) and its amax for the next layer
+            Ld["layer"].forward(self.x, Ld["ids"], Ld["w"], self.res, in_amax=self.amax, accumulate=True,
+                                mark=mark if li == 0 else None, x_next=self.x, amax_next=self.amax)
 
     def value(self, seconds_per_step):
         return self.units_per_step / seconds_per_step

@@ -249,6 +249,8 @@ def _moe_sigs():
                                       ctypes.c_int, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_forward": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float, _P,
                                 _P, ctypes.c_int, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_forward_chain": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts),
+                                      ctypes.c_float, _P, _P, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_calibrate": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float,
                                   _P, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_workspace_view": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -348,17 +350,23 @@ MOE_ACCUMULATE, MOE_ATOMIC = 1, 2
 
 
 def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: float | None = None, in_amax=None,
-                out=None, accumulate: bool = False, atomic: bool = False, stream=None):
-    """MoE layer (dispatch -> gate/up -> down + combine) -> out [T, H] fp32."""
+                out=None, accumulate: bool = False, atomic: bool = False, x_next=None, amax_next=None, stream=None):
+    """MoE layer (dispatch -> gate/up -> down + combine) -> out [T, H] fp32.  With x_next (bf16 [T, H]) and amax_next
+    (fp32 [1]) the combine also writes bf16(out) and its max |.| there (nvfp4b_moe_forward_chain)."""
     T = x.shape[0]
     topk = ids.shape[1]
     if out is None:
         out = torch.empty((T, experts.H), dtype=torch.float32, device=x.device)
     st = experts.struct()
+    flags = (MOE_ACCUMULATE if accumulate else 0) | (MOE_ATOMIC if atomic else 0)
+    if x_next is not None:
+        _check("moe_forward_chain", _moe_sigs().nvfp4b_moe_forward_chain(
+            _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
+            _ptr(out), flags, _ptr(workspace), _ptr(x_next), _ptr(amax_next), _stream(stream)))
+        return out
     _check("moe_forward", _moe_sigs().nvfp4b_moe_forward(
         _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
-        _ptr(out), (MOE_ACCUMULATE if accumulate else 0) | (MOE_ATOMIC if atomic else 0),
-        _ptr(workspace), _stream(stream)))
+        _ptr(out), flags, _ptr(workspace), _stream(stream)))
     return out
 
 
@@ -503,6 +511,8 @@ def _p2p_sigs():
         "nvfp4b_ep_p2p_expert_forward": ([ctypes.POINTER(_Experts), _P, PP, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_combine": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, PP, _P,
                                    ctypes.c_int, _P], ctypes.c_int),
+        "nvfp4b_ep_p2p_combine_chain": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, PP, _P,
+                                         ctypes.c_int, _P, _P, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_state": ([PP, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_recv_counts": ([PP, _P], ctypes.c_int),
         "nvfp4b_ipc_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
@@ -587,10 +597,16 @@ def ep_p2p_expert_forward(experts: MoeExperts, workspace, peers: EpPeers, stream
 
 
 def ep_p2p_combine(T: int, topk: int, E: int, workspace, peers: EpPeers, out, accumulate: bool = False,
-                   stream=None):
-    """Source side over peer memory: waits for the rows, slot-ordered sum into out."""
+                   x_next=None, amax_next=None, stream=None):
+    """Source side over peer memory: waits for the rows, slot-ordered sum into out (+ the chained bf16 copy and
+    amax when x_next / amax_next are given)."""
     H = out.shape[1]
+    flags = MOE_ACCUMULATE if accumulate else 0
+    if x_next is not None:
+        _check("ep_p2p_combine_chain", _p2p_sigs().nvfp4b_ep_p2p_combine_chain(
+            T, H, topk, E, _ptr(workspace), ctypes.byref(peers), _ptr(out), flags, _ptr(x_next), _ptr(amax_next),
+            _stream(stream)))
+        return out
     _check("ep_p2p_combine", _p2p_sigs().nvfp4b_ep_p2p_combine(
-        T, H, topk, E, _ptr(workspace), ctypes.byref(peers), _ptr(out), MOE_ACCUMULATE if accumulate else 0,
-        _stream(stream)))
+        T, H, topk, E, _ptr(workspace), ctypes.byref(peers), _ptr(out), flags, _stream(stream)))
     return out

@@ -645,32 +645,69 @@ struct DownEpi {
     }
 };
 
+// Optional second output of the combine kernels, for a stack of layers on a residual stream: the finished row
+// rounded to bf16 (RNE) into x (the next layer's input) and max |x| into *amax (its dynamic activation scale, a
+// float ordered by its bit pattern; zeroed by the host entry just before the combine).  x == nullptr: off.
+struct CombineNext {
+    uint16_t* x;
+    float* amax;
+};
+
+// Every thread of the block calls this (it ends with a block barrier when nx.x is set).
+__device__ __forceinline__ void combine_next(const CombineNext& nx, bool valid, long long off, const float (&acc)[8]) {
+    if (!nx.x) return;                               // kernel-uniform
+    uint32_t m = 0;
+    if (valid) {
+        uint32_t b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+            b[i] = *reinterpret_cast<const uint32_t*>(&h);
+            m = __vmaxu2(m, b[i] & 0x7FFF7FFFu);
+        }
+        *reinterpret_cast<uint4*>(nx.x + off) = make_uint4(b[0], b[1], b[2], b[3]);
+    }
+    __shared__ uint32_t red[32];
+    uint32_t m16 = max(m & 0xFFFFu, m >> 16);
+    m16 = __reduce_max_sync(0xFFFFFFFFu, m16);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m16;
+    __syncthreads();
+    if (threadIdx.x < 32) {                          // one atomic per block (same-address atomics serialise)
+        uint32_t v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0u;
+        v = __reduce_max_sync(0xFFFFFFFFu, v);
+        if (threadIdx.x == 0 && v != 0) atomicMax(reinterpret_cast<unsigned*>(nx.amax), v << 16);
+    }
+}
+
 // out[t] (+)= sum_j y[t*k + j] over the k slots in order, fp32 accumulation of the fp16 rows.  One thread per
 // (token, 8 columns): T * H / 8 independent 16-byte gathers; H % 8 == 0.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const uint16_t* __restrict__ y, int T, int H, int topk,
-                                                          float* __restrict__ out, int accumulate) {
+                                                          float* __restrict__ out, int accumulate,
+                                                          const CombineNext next) {
     const int chunks = H >> 3;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long long)T * chunks) return;
-    const int t = (int)(idx / chunks), c = (int)(idx - (long long)t * chunks) * 8;
-    const uint16_t* src = y + (long long)t * topk * H + c;
-    float* dst = out + (long long)t * H + c;
+    const bool valid = idx < (long long)T * chunks;
+    const int t = valid ? (int)(idx / chunks) : 0, c = valid ? (int)(idx - (long long)t * chunks) * 8 : 0;
     float acc[8];
-    if (accumulate) {
-        const float4 u = *reinterpret_cast<const float4*>(dst), v = *reinterpret_cast<const float4*>(dst + 4);
-        acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
-    } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    if (valid) {
+        const uint16_t* src = y + (long long)t * topk * H + c;
+        float* dst = out + (long long)t * H + c;
+        if (accumulate) {
+            const float4 u = *reinterpret_cast<const float4*>(dst), v = *reinterpret_cast<const float4*>(dst + 4);
+            acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
+        }
+        for (int j = 0; j < topk; ++j) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + (long long)j * H));
+            const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
+            acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+            acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+        }
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
-    for (int j = 0; j < topk; ++j) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + (long long)j * H));
-        const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
-        acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
-        acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
-    }
-    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    combine_next(next, valid, (long long)t * H + c, acc);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -848,31 +885,33 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
 __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back, int T, int H, int topk,
                                                          const int* __restrict__ slot, float* __restrict__ out,
                                                          int accumulate, const unsigned* wait_flags, int G,
-                                                         const unsigned* state, int* err) {
+                                                         const unsigned* state, int* err, const CombineNext next) {
     if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err);
     const int chunks = H >> 3;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long long)T * chunks) return;
-    const int t = (int)(idx / chunks), c = (int)(idx - (long long)t * chunks) * 8;
-    float* dst = out + (long long)t * H + c;
+    const bool valid = idx < (long long)T * chunks;
+    const int t = valid ? (int)(idx / chunks) : 0, c = valid ? (int)(idx - (long long)t * chunks) * 8 : 0;
     float acc[8];
-    if (accumulate) {
-        const float4 u = *reinterpret_cast<const float4*>(dst), v = *reinterpret_cast<const float4*>(dst + 4);
-        acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
-    } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    if (valid) {
+        float* dst = out + (long long)t * H + c;
+        if (accumulate) {
+            const float4 u = *reinterpret_cast<const float4*>(dst), v = *reinterpret_cast<const float4*>(dst + 4);
+            acc[0] = u.x; acc[1] = u.y; acc[2] = u.z; acc[3] = u.w; acc[4] = v.x; acc[5] = v.y; acc[6] = v.z; acc[7] = v.w;
+        }
+        for (int j = 0; j < topk; ++j) {
+            const int r = __ldg(slot + (long long)t * topk + j);
+            if (r < 0) continue;
+            const uint4 q = *reinterpret_cast<const uint4*>(y_back + (long long)r * H + c);
+            const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
+            acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
+            acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
+        }
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
-    for (int j = 0; j < topk; ++j) {
-        const int r = __ldg(slot + (long long)t * topk + j);
-        if (r < 0) continue;
-        const uint4 q = *reinterpret_cast<const uint4*>(y_back + (long long)r * H + c);
-        const float2 f0 = unpack_half2(q.x), f1 = unpack_half2(q.y), f2 = unpack_half2(q.z), f3 = unpack_half2(q.w);
-        acc[0] += f0.x; acc[1] += f0.y; acc[2] += f1.x; acc[3] += f1.y;
-        acc[4] += f2.x; acc[5] += f2.y; acc[6] += f3.x; acc[7] += f3.y;
-    }
-    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    combine_next(next, valid, (long long)t * H + c, acc);
 }
 
 using GroupCfg = KCfg<256, 4, 1, 8>;
@@ -953,7 +992,8 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
 }
 
 int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, float* out, int flags,
-         const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr) {
+         const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr,
+         const CombineNext next = CombineNext{nullptr, nullptr}) {
     const bool accumulate = (flags & NVFP4B_MOE_ACCUMULATE) != 0;
     const bool deterministic = (flags & NVFP4B_MOE_ATOMIC) == 0;
     const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
@@ -990,8 +1030,12 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
         }
         st = launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
         if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
+        if (next.x) {
+            const cudaError_t err = cudaMemsetAsync(next.amax, 0, sizeof(float), s);
+            if (err != cudaSuccess) return record_cuda_error(err);
+        }
         moe_combine_kernel<<<(unsigned)(((long long)T * (H / 8) + 255) / 256), 256, 0, s>>>(w.y, T, H, topk, out,
-                                                                                      accumulate ? 1 : 0);
+                                                                                      accumulate ? 1 : 0, next);
         return launch_status();
     }
     if (!accumulate) {
@@ -1275,20 +1319,37 @@ static int moe_common_checks(const void* x, int T, const int* ids, const float* 
     return NVFP4B_OK;
 }
 
-extern "C" int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
-                                  const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax, float* out,
-                                  int flags, void* workspace, void* stream) {
+static int moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
+                       const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax, float* out, int flags,
+                       void* workspace, const CombineNext next, void* stream) {
     int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
     if (st) return st;
     if (!out) return NVFP4B_ERR_NULL;
-    if (!aligned16(out)) return NVFP4B_ERR_ALIGN;
+    if (!aligned16(out) || (next.x && !aligned16(next.x))) return NVFP4B_ERR_ALIGN;
+    if (next.x && (flags & NVFP4B_MOE_ATOMIC)) return NVFP4B_ERR_ARG;     // the chained output needs the combine
     cudaStream_t s = (cudaStream_t)stream;
     const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
     st = dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w, s);
     if (st) return st;
     st = gate_up<false>(ex, T, topk, in_gscale, d_in_amax, nullptr, w, s);
     if (st) return st;
-    return down(ex, T, topk, weights, out, flags, w, s);
+    return down(ex, T, topk, weights, out, flags, w, s, nullptr, next);
+}
+
+extern "C" int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
+                                  const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax, float* out,
+                                  int flags, void* workspace, void* stream) {
+    return moe_forward(x, T, ids, weights, topk, ex, in_gscale, d_in_amax, out, flags, workspace,
+                       CombineNext{nullptr, nullptr}, stream);
+}
+
+extern "C" int nvfp4b_moe_forward_chain(const void* x, int T, const int* ids, const float* weights, int topk,
+                                        const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax,
+                                        float* out, int flags, void* workspace, void* x_next, float* d_amax_next,
+                                        void* stream) {
+    if (!x_next || !d_amax_next) return NVFP4B_ERR_NULL;
+    return moe_forward(x, T, ids, weights, topk, ex, in_gscale, d_in_amax, out, flags, workspace,
+                       CombineNext{static_cast<uint16_t*>(x_next), d_amax_next}, stream);
 }
 
 extern "C" int nvfp4b_moe_dispatch(const void* x, int T, const int* ids, const float* weights, int topk,
@@ -1394,7 +1455,8 @@ extern "C" int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk,
     const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
     const long long threads = (long long)T * (H / 8);
     ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, nullptr, 0, nullptr, nullptr);
+        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, nullptr, 0, nullptr, nullptr,
+        CombineNext{nullptr, nullptr});
     return launch_status();
 }
 
@@ -1458,22 +1520,40 @@ extern "C" int nvfp4b_ep_p2p_expert_forward(const nvfp4b_moe_experts* ex, void* 
                      peers);
 }
 
-extern "C" int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace,
-                                     const nvfp4b_ep_peers* peers, float* out, int flags, void* stream) {
+static int ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
+                          float* out, int flags, const CombineNext next, void* stream) {
     if (!workspace || !out) return NVFP4B_ERR_NULL;
     const int st = check_peers(peers);
     if (st) return st;
     if (T <= 0 || H <= 0 || (H % 256) || topk <= 0 || topk > 16 || E <= 0) return NVFP4B_ERR_SHAPE;
     if (flags & ~NVFP4B_MOE_ACCUMULATE) return NVFP4B_ERR_ARG;
-    if (!aligned16(out)) return NVFP4B_ERR_ALIGN;
+    if (!aligned16(out) || (next.x && !aligned16(next.x))) return NVFP4B_ERR_ALIGN;
     int* err = device_error_ptr();
     if (!err) return NVFP4B_ERR_CUDA;
+    const cudaStream_t s = (cudaStream_t)stream;
+    if (next.x) {
+        const cudaError_t e = cudaMemsetAsync(next.amax, 0, sizeof(float), s);
+        if (e != cudaSuccess) return record_cuda_error(e);
+    }
     const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
     const long long threads = (long long)T * (H / 8);
-    ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+    ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
         peers->my_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, peers->my_flags + peers->G,
-        peers->G, peers->state, err);
+        peers->G, peers->state, err, next);
     return launch_status();
+}
+
+extern "C" int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace,
+                                     const nvfp4b_ep_peers* peers, float* out, int flags, void* stream) {
+    return ep_p2p_combine(T, H, topk, E, workspace, peers, out, flags, CombineNext{nullptr, nullptr}, stream);
+}
+
+extern "C" int nvfp4b_ep_p2p_combine_chain(int T, int H, int topk, int E, const void* workspace,
+                                           const nvfp4b_ep_peers* peers, float* out, int flags, void* x_next,
+                                           float* d_amax_next, void* stream) {
+    if (!x_next || !d_amax_next) return NVFP4B_ERR_NULL;
+    return ep_p2p_combine(T, H, topk, E, workspace, peers, out, flags,
+                          CombineNext{static_cast<uint16_t*>(x_next), d_amax_next}, stream);
 }
 
 extern "C" int nvfp4b_ep_p2p_state(const nvfp4b_ep_peers* peers, unsigned* host_words4) {

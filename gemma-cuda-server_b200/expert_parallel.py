@@ -170,9 +170,9 @@ class P2PKernelOps:
     def expert(self):
         self.pkg.ep_p2p_expert_forward(self.experts, self.exp_ws, self.ex.peers)
 
-    def combine(self, out, accumulate: bool):
+    def combine(self, out, accumulate: bool, x_next=None, amax_next=None):
         return self.pkg.ep_p2p_combine(self.T, self.topk, self.E, self.src_ws, self.ex.peers, out,
-                                       accumulate=accumulate)
+                                       accumulate=accumulate, x_next=x_next, amax_next=amax_next)
 
 
 class LocalOps:
@@ -190,11 +190,12 @@ class LocalOps:
         self.src_ws = pkg.moe_workspace(T_cap, experts.H, experts.I, E, topk, device=device)
         self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
 
-    def layer(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False):
+    def layer(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False, x_next=None,
+              amax_next=None):
         if x.shape[0] > self.T_cap:
             raise ValueError(f"{x.shape[0]} tokens exceed the capacity {self.T_cap}")
         return self.pkg.moe_forward(x, ids, weights, self.experts, self.src_ws, in_gscale=in_gscale, in_amax=in_amax,
-                                    out=out, accumulate=accumulate)
+                                    out=out, accumulate=accumulate, x_next=x_next, amax_next=amax_next)
 
 
 class ExpertParallelMoE:
@@ -206,14 +207,18 @@ class ExpertParallelMoE:
         if self.G > 1 and dist.get_world_size(group) != self.G:
             raise ValueError("ops were built for a different group size")
 
-    def forward(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False, mark=None):
-        """out[t] (+)= the layer's output for token t.  `mark(name)`, if given, is called around the expert-side
-        kernels ("kernel" / "kernel_end") so a caller can time them with events on the current stream."""
+    def forward(self, x, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False, mark=None,
+                x_next=None, amax_next=None):
+        """out[t] (+)= the layer's output for token t.  With x_next (bf16, may be x itself) and amax_next (fp32 [1],
+        may be in_amax) also x_next = bf16(out) and amax_next = max |x_next|: the next layer's input on a residual
+        stream, fused into the combine where the path has it.  `mark(name)`, if given, is called around the
+        expert-side kernels ("kernel" / "kernel_end") so a caller can time them with events on the current stream."""
         ops, G, grp = self.ops, self.G, self.group
         if getattr(ops, "local", False):
             if mark is not None:
                 mark("kernel")
-            ops.layer(x, ids, weights, out, in_gscale=in_gscale, in_amax=in_amax, accumulate=accumulate)
+            ops.layer(x, ids, weights, out, in_gscale=in_gscale, in_amax=in_amax, accumulate=accumulate,
+                      x_next=x_next, amax_next=amax_next)
             if mark is not None:
                 mark("kernel_end")
             return out
@@ -224,7 +229,7 @@ class ExpertParallelMoE:
             ops.expert()
             if mark is not None:
                 mark("kernel_end")
-            return ops.combine(out, accumulate)
+            return ops.combine(out, accumulate, x_next=x_next, amax_next=amax_next)
         send_counts, recv_counts = ops.dispatch(x, ids, weights, in_gscale=in_gscale, in_amax=in_amax)
         if G > 1:
             dist.all_to_all_single(recv_counts, send_counts, group=grp)
@@ -243,7 +248,11 @@ class ExpertParallelMoE:
             back = ops.back
         else:
             back = rows
-        return ops.combine(back, out, accumulate)
+        ops.combine(back, out, accumulate)
+        if x_next is not None:
+            x_next.copy_(out)
+            ops.pkg.amax(x_next, out=amax_next)
+        return out
 
     def overflowed(self, reset: bool = True) -> bool:
         """True if a layer since the last reset had more than `capacity` records for one rank pair (host read)."""

@@ -197,6 +197,14 @@ int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weight
                        const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
                        int flags, void* workspace, void* stream);
 
+/* nvfp4b_moe_forward for a stack of layers on a residual stream: the combine also writes each finished out row
+ * rounded to bf16 (RNE) into x_next [T, H] and max |x_next| into *d_amax_next (zeroed by this call after the layer
+ * has read its own inputs, so x_next/d_amax_next may be the layer's own x/d_in_amax).  That is the next layer's
+ * input and dynamic-scale amax, without a separate cast and amax pass.  NVFP4B_MOE_ATOMIC is not allowed here. */
+int nvfp4b_moe_forward_chain(const void* x, int T, const int* ids, const float* weights, int topk,
+                             const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
+                             int flags, void* workspace, void* x_next, float* d_amax_next, void* stream);
+
 /* The three stages of nvfp4b_moe_forward, callable one by one (same stream, same workspace, in this order):
  * dispatch (plan + quantise-scatter of x), gate/up grouped GEMM (writes the NVFP4 intermediate), down grouped GEMM
  * + weighted combine into out (flags as for nvfp4b_moe_forward). */
@@ -329,6 +337,11 @@ int nvfp4b_ep_p2p_expert_forward(const nvfp4b_moe_experts* experts, void* worksp
  * NVFP4B_MOE_ACCUMULATE or 0).  `workspace` is the one given to nvfp4b_ep_p2p_dispatch. */
 int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
                           float* out, int flags, void* stream);
+
+/* nvfp4b_ep_p2p_combine plus the chained outputs of nvfp4b_moe_forward_chain (bf16 copy of the finished rows into
+ * x_next, their max |.| into *d_amax_next, zeroed by this call). */
+int nvfp4b_ep_p2p_combine_chain(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
+                                float* out, int flags, void* x_next, float* d_amax_next, void* stream);
 
 /* Debug reads (synchronous, not for capture): a rank's private words (layer epoch, completion counters, spare) and
  * its receive counts [G] (records from each source in the last layer). */

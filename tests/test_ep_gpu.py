@@ -154,3 +154,59 @@ def test_ep_p2p_overflow_is_flagged():
     finally:
         for e in ex:
             e.close()
+
+
+# ---- chained outputs of the combine (residual stream: the next layer's bf16 input and its amax) -----------------
+
+def test_moe_forward_chain_outputs():
+    """nvfp4b_moe_forward_chain: out as nvfp4b_moe_forward, plus x_next = bf16(out) and amax_next = max |x_next|,
+    also when x_next / amax_next are the layer's own x / amax (in place)."""
+    p, P = make_problem(200, 512, 128, 32, 8, seed=67)
+    ids, w, _, _ = route_and_calibrate(p, P)
+    amax = p.amax(P["x"])
+    base = torch.randn((200, 512), device="cuda")
+    ref = p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_amax=amax, out=base.clone(), accumulate=True)
+    ref_x = ref.to(torch.bfloat16)
+    ref_a = ref_x.float().abs().max()
+    out, xn, an = base.clone(), torch.empty_like(P["x"]), torch.full((1,), 123.0, device="cuda")
+    p.moe_forward(P["x"], ids, w, P["arena"], P["ws"], in_amax=amax, out=out, accumulate=True, x_next=xn,
+                  amax_next=an)
+    x2, a2, out2 = P["x"].clone(), amax.clone(), base.clone()
+    p.moe_forward(x2, ids, w, P["arena"], P["ws"], in_amax=a2, out=out2, accumulate=True, x_next=x2, amax_next=a2)
+    torch.cuda.synchronize()
+    assert p.read_device_error() == 0
+    assert torch.equal(out, ref) and torch.equal(xn, ref_x) and an.item() == ref_a.item()
+    assert torch.equal(out2, ref) and torch.equal(x2, ref_x) and a2.item() == ref_a.item()
+
+
+def test_ep_p2p_combine_chain_outputs():
+    """The peer-memory combine with the chained outputs, G = 2 emulated: same out, x_next = bf16(out), amax."""
+    import gemma_cuda_server_b200.expert_parallel as epm
+    G, T = 2, 96
+    p, P = make_problem(T * G, 512, 128, 32, 8, seed=71)
+    P["ids"], P["w"], _, _ = route_and_calibrate(p, P)
+    E, k, H = P["E"], P["topk"], P["H"]
+    ex = epm.PeerExchange.local_group(p, G, epm.P2PKernelOps.default_capacity(T, k, G), H)
+    try:
+        ops = [epm.P2PKernelOps(p, P["arena"].slice(r * E // G, (r + 1) * E // G), E, k, T, ex[r]) for r in range(G)]
+        xs = [P["x"][r * T:(r + 1) * T].clone() for r in range(G)]
+        amaxes = [p.amax(x) for x in xs]
+        refs = [p.moe_forward(xs[r], P["ids"][r * T:(r + 1) * T].contiguous(), P["w"][r * T:(r + 1) * T].contiguous(),
+                              P["arena"], P["ws"], in_amax=amaxes[r]).clone() for r in range(G)]
+        outs = [torch.zeros((T, H), device="cuda") for _ in range(G)]
+        for r in range(G):
+            ops[r].dispatch(xs[r], P["ids"][r * T:(r + 1) * T].contiguous(), P["w"][r * T:(r + 1) * T].contiguous(),
+                            in_amax=amaxes[r])
+        for r in range(G):
+            ops[r].expert()
+        for r in range(G):                       # in place: the rank's own x and amax become the next layer's
+            ops[r].combine(outs[r], True, x_next=xs[r], amax_next=amaxes[r])
+        torch.cuda.synchronize()
+        assert p.read_device_error() == 0
+        for r in range(G):
+            assert torch.equal(outs[r], refs[r])
+            assert torch.equal(xs[r], refs[r].to(torch.bfloat16))
+            assert amaxes[r].item() == refs[r].to(torch.bfloat16).float().abs().max().item()
+    finally:
+        for e in ex:
+            e.close()
