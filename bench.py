@@ -63,6 +63,8 @@ def parse_args():
                          "(nccl), the single-GPU MoE layer (local, 1 GPU only), or auto = p2p on 2+ GPUs, local on 1")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
+    ap.add_argument("--cuda-profiler-range", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return ap.parse_args()
 
 
@@ -695,6 +697,8 @@ def main():
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         marks = [{} for _ in range(args.steps)]
+        if args.cuda_profiler_range:
+            torch.cuda.profiler.start()
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
@@ -709,6 +713,8 @@ def main():
                 W.step(mark)
             stops[i].record(stream)
         barrier()
+        if args.cuda_profiler_range:
+            torch.cuda.profiler.stop()
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
         if graph is not None:          # kernel marks from eager steps (events cannot be taken inside the replay)
             marks = [{} for _ in range(3)]

@@ -255,11 +255,21 @@ __global__ void __launch_bounds__(256) moe_plan_kernel(const int* __restrict__ h
     int total = 0;
     if (e < E)
         for (int c = 0; c < n_chunks; ++c) total += hist[c * E + e];
-    padded[e + 1] = (e < E) ? (total + 127) / 128 * 128 : 0;
-    if (e == 0) padded[0] = 0;
+    // inclusive scan of the padded segment sizes (warp scans, then the 8 warp totals) -> padded[e + 1] = end of e
+    __shared__ int wsum[8];
+    const int lane = e & 31, wid = e >> 5;
+    int v = (e < E) ? (total + 127) / 128 * 128 : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) wsum[wid] = v;
     __syncthreads();
-    if (e == 0)
-        for (int i = 1; i <= E; ++i) padded[i] += padded[i - 1];   // inclusive scan -> starts
+    int off = 0;
+    for (int q = 0; q < wid; ++q) off += wsum[q];
+    padded[e + 1] = v + off;
+    if (e == 0) padded[0] = 0;
     __syncthreads();
     if (e < E) {
         const int start = padded[e];
@@ -330,12 +340,11 @@ __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ se
     const int e = blockIdx.x;
     const int start = seg_start[e], count = seg_count[e];
     const int pad0 = start + count, pad1 = start + (count + 127) / 128 * 128;
-    const int n = (pad1 - pad0) * tile_cols;          // one 4-byte word = 4 blocks of one row per store
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int r = pad0 + i / tile_cols, tc = i % tile_cols;
-        *reinterpret_cast<uint32_t*>(a_scales + ((long long)(r >> 7) * tile_cols + tc) * 512 + (r & 31) * 16 +
-                                     ((r & 127) >> 5) * 4) = 0u;
-        if (tc == 0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = pad0 + warp; r < pad1; r += 8) {      // warp per padding row, lanes along its 4-block scale words
+        uint8_t* row_sf = a_scales + (long long)(r >> 7) * tile_cols * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
+        for (int tc = lane; tc < tile_cols; tc += 32) *reinterpret_cast<uint32_t*>(row_sf + (long long)tc * 512) = 0u;
+        if (lane == 0) {
             row_token[r] = -1;
             row_weight[r] = 0.f;
             row_assign[r] = -1;
