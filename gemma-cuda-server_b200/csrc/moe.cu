@@ -609,20 +609,50 @@ struct DownEpi {
         }
     }
 
-    // DETERMINISTIC: each lane converts its row's 32-column chunk to fp16 and stores it as four 16-byte pieces (64
-    // contiguous bytes of the row); no shared-memory transpose, so the epilogue's per-tile cost -- which bounds this
-    // short-K GEMM -- is a handful of instructions per chunk.
+    // DETERMINISTIC, rows to local memory: each lane converts its row's 32-column chunk to fp16 and stores it as four
+    // 16-byte pieces (64 contiguous bytes of the row); no shared-memory transpose, so the epilogue's per-tile cost --
+    // which bounds this short-K GEMM -- is a handful of instructions per chunk.
+    // DETERMINISTIC, rows to peer memory (peer_back): 16-byte pieces of 32 different rows per store instruction cost
+    // NVLink packets of half a 32-byte sector each, so there each warp first transposes its 32 x 32 chunk through
+    // shared memory (32 x 33 floats, the EPI_SMEM of DownPeerCfg) and every store instruction writes four whole
+    // 64-byte row segments.
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
-                                            uint8_t*) const {
+                                            uint8_t* esm) const {
         const long long m = (long long)ti.a_row + row;
         const int a = __ldg(row_assign + m);
         const int e = ti.expert;
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
+            if (peer_back) {
+                const int lane = threadIdx.x & 31;
+                uint16_t* rowp = a >= 0 ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
+                                        : nullptr;
+                float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 4) * (32 * 33);   // warps 4..
+                const int sub = lane >> 3, q = (lane & 7) * 4;
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    const int n0 = ti.n0 + col_base + 32 * c;   // warp-uniform
+                    if (n0 >= H) continue;
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = s * __uint_as_float(r[c][i]);
+                    __syncwarp();
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        const int i = 4 * g + sub;
+                        uint16_t* pi = reinterpret_cast<uint16_t*>(
+                            __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), i));
+                        const float* src = tile + i * 33 + q;
+                        if (pi)
+                            *reinterpret_cast<uint2*>(pi + n0 + q) =
+                                make_uint2(pack_half2_sat(src[0], src[1]), pack_half2_sat(src[2], src[3]));
+                    }
+                }
+                return;
+            }
             if (a < 0) return;
-            uint16_t* rowp = peer_back ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
-                                       : y + (long long)a * H;
+            uint16_t* rowp = y + (long long)a * H;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
                 const int n0 = ti.n0 + col_base + 32 * c;
@@ -925,6 +955,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back,
 
 using GroupCfg = KCfg<256, 4, 1, 8>;
 using DownCfg = KCfg<256, 4, 1, 8>;   // K = I is short: the epilogue bounds it (direct fp16 row stores)
+using DownPeerCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // rows to peer memory: + transpose tiles
 
 // ---------------------------------------------------------------------------------------------------------------
 // host orchestration
@@ -1037,7 +1068,9 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
             e.G = peers->G;
             e.capacity = peers->capacity;
         }
-        st = launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
+        static_assert(DownPeerCfg::BM == DownCfg::BM && DownPeerCfg::BN == DownCfg::BN, "same tiles, same maps");
+        st = peers ? launch_core<DownPeerCfg>(ma, mb, cp, sc, e, sm_count(), s)
+                   : launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
         if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
         if (next.x) {
             const cudaError_t err = cudaMemsetAsync(next.amax, 0, sizeof(float), s);
