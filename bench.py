@@ -387,8 +387,10 @@ class MoeWorkload:
 class EpWorkload:
     """cfg4: expert-parallel decode/verify stack on G GPUs -- 30 stacked MoE FFN layers shaped as cfg3 (H=2816,
     128 experts of I=704, top-8), 512 rows (32 sequences x 16 draft tokens) per rank per step, experts sharded
-    128/G per GPU, NCCL all-to-all of the routed records and of the returned rows per layer.  Layers are chained
-    through an fp32 residual stream (each layer adds its MoE output, the next layer reads it back as bf16)."""
+    128/G per GPU.  Exchange per layer: routed records and returned rows stored into the other ranks' memory over
+    NVLink by the kernels (p2p, default on 2+ GPUs), or NCCL all-to-all (nccl); one GPU runs the single-GPU layer
+    (local).  Layers are chained through an fp32 residual stream: each layer adds its MoE output, and its combine
+    also leaves the next layer's bf16 input and amax."""
     name = "ep"
     unit = "tokens/s"
     dtype = "nvfp4"
