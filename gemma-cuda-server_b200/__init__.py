@@ -249,6 +249,8 @@ def _moe_sigs():
                                       ctypes.c_int, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_forward": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float, _P,
                                 _P, ctypes.c_int, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_forward_norm": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), _P,
+                                     ctypes.c_float, ctypes.c_float, _P, ctypes.c_int, _P, _P], ctypes.c_int),
         "nvfp4b_moe_forward_chain": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts),
                                       ctypes.c_float, _P, _P, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_calibrate": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float,
@@ -367,6 +369,21 @@ def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: floa
     _check("moe_forward", _moe_sigs().nvfp4b_moe_forward(
         _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
         _ptr(out), flags, _ptr(workspace), _stream(stream)))
+    return out
+
+
+def moe_forward_norm(x, ids, weights, experts: MoeExperts, workspace, norm_weight, in_gscale: float,
+                     eps: float = 1e-6, out=None, accumulate: bool = False, stream=None):
+    """MoE layer whose input rows are RMS-normalised (x * rsqrt(mean(x^2) + eps) * norm_weight, fp32) inside the
+    quantise-dispatch; static activation global scale in_gscale."""
+    T = x.shape[0]
+    topk = ids.shape[1]
+    if out is None:
+        out = torch.empty((T, experts.H), dtype=torch.float32, device=x.device)
+    st = experts.struct()
+    _check("moe_forward_norm", _moe_sigs().nvfp4b_moe_forward_norm(
+        _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), _ptr(norm_weight), float(eps),
+        float(in_gscale), _ptr(out), MOE_ACCUMULATE if accumulate else 0, _ptr(workspace), _stream(stream)))
     return out
 
 

@@ -361,12 +361,16 @@ __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ se
 constexpr int kScatterWarps = 6;   // warps per token in the quantise-and-scatter kernel (6 x 32 lanes >= H/16 = 176)
 
 // kScatterWarps warps per token: warp `part` quantises every kScatterWarps-th run of 32 blocks of x[t] once and
-// writes each block to all of the token's destination rows.
+// writes each block to all of the token's destination rows.  With norm_w (bf16 [H]) the row is RMS-normalised first,
+// x * rsqrt(mean(x^2) + eps) * norm_w in fp32 (the reference's rmsnorm, kernels/elementwise.cu:10-22, applied to
+// the MoE input as pre_feedforward_layernorm_2 in src/forward.cu:535), and the fp32 values are quantised: the
+// normalised activations are never stored.
 __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* __restrict__ x, int T, int H,
                                                                 int topk, const int* __restrict__ dest,
                                                                 float gscale, const float* __restrict__ d_amax,
                                                                 uint8_t* __restrict__ a_codes,
-                                                                uint8_t* __restrict__ a_scales, int tile_cols) {
+                                                                uint8_t* __restrict__ a_scales, int tile_cols,
+                                                                const uint16_t* __restrict__ norm_w, float eps) {
     const int lane = threadIdx.x & 31;
     const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     const int t = gw / kScatterWarps, part = gw % kScatterWarps;
@@ -375,6 +379,23 @@ __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* 
     const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
     const int kb = H >> 4;
     const uint16_t* xr = x + (long long)t * H;
+    float inv = 1.f;
+    if (norm_w) {                                    // every warp of the token reduces the whole row (L1-resident)
+        float ss = 0.f;
+        for (int k = lane * 8; k < H; k += 256) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + k));
+            const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float a = bf16lo(w4[i]), b = bf16hi(w4[i]);
+                ss = fmaf(a, a, ss);
+                ss = fmaf(b, b, ss);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        inv = rsqrtf(ss / (float)H + eps);
+    }
     for (int b0 = part * 32; b0 < kb; b0 += 32 * kScatterWarps) {
         const int b = b0 + lane;
         uint32_t w0 = 0, w1 = 0, sf = 0;
@@ -382,7 +403,20 @@ __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* 
             const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
             const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
             const uint32_t ww[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-            sf = quantize16_bf16(ww, g, w0, w1);
+            if (norm_w) {
+                const uint4 n0 = __ldg(reinterpret_cast<const uint4*>(norm_w + b * 16));
+                const uint4 n1 = __ldg(reinterpret_cast<const uint4*>(norm_w + b * 16) + 1);
+                const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+                float v[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    v[2 * i] = __fmul_rn(__fmul_rn(bf16lo(ww[i]), inv), bf16lo(nw[i]));
+                    v[2 * i + 1] = __fmul_rn(__fmul_rn(bf16hi(ww[i]), inv), bf16hi(nw[i]));
+                }
+                sf = quantize16(v, g, w0, w1);
+            } else {
+                sf = quantize16_bf16(ww, g, w0, w1);
+            }
         }
         for (int j = 0; j < topk; ++j) {
             const int r = __shfl_sync(0xFFFFFFFFu, my_dest, j);
@@ -974,7 +1008,8 @@ int check_experts(const nvfp4b_moe_experts* ex) {
 }
 
 int dispatch(const void* x, int T, const int* ids, const float* weights, int topk, int H, int E, float in_gscale,
-             const float* d_in_amax, const Workspace& w, cudaStream_t s) {
+             const float* d_in_amax, const Workspace& w, cudaStream_t s, const uint16_t* norm_w = nullptr,
+             float eps = 0.f) {
     const int n_assign = T * topk;
     const int n_chunks = (n_assign + kChunk - 1) / kChunk;
     moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
@@ -986,7 +1021,8 @@ int dispatch(const void* x, int T, const int* ids, const float* weights, int top
     moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
                                      w.row_weight, w.row_assign, nullptr);
     moe_quant_scatter_kernel<<<(T * kScatterWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
-                                                         in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols);
+                                                         in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols,
+                                                         norm_w, eps);
     return launch_status();
 }
 
@@ -1363,7 +1399,8 @@ static int moe_common_checks(const void* x, int T, const int* ids, const float* 
 
 static int moe_forward(const void* x, int T, const int* ids, const float* weights, int topk,
                        const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax, float* out, int flags,
-                       void* workspace, const CombineNext next, void* stream) {
+                       void* workspace, const CombineNext next, void* stream, const uint16_t* norm_w = nullptr,
+                       float eps = 0.f) {
     int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
     if (st) return st;
     if (!out) return NVFP4B_ERR_NULL;
@@ -1371,7 +1408,7 @@ static int moe_forward(const void* x, int T, const int* ids, const float* weight
     if (next.x && (flags & NVFP4B_MOE_ATOMIC)) return NVFP4B_ERR_ARG;     // the chained output needs the combine
     cudaStream_t s = (cudaStream_t)stream;
     const Workspace w = carve(workspace, T, ex->hidden, ex->inter, ex->num_experts, topk);
-    st = dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w, s);
+    st = dispatch(x, T, ids, weights, topk, ex->hidden, ex->num_experts, in_gscale, d_in_amax, w, s, norm_w, eps);
     if (st) return st;
     st = gate_up<false>(ex, T, topk, in_gscale, d_in_amax, nullptr, w, s);
     if (st) return st;
@@ -1383,6 +1420,16 @@ extern "C" int nvfp4b_moe_forward(const void* x, int T, const int* ids, const fl
                                   int flags, void* workspace, void* stream) {
     return moe_forward(x, T, ids, weights, topk, ex, in_gscale, d_in_amax, out, flags, workspace,
                        CombineNext{nullptr, nullptr}, stream);
+}
+
+extern "C" int nvfp4b_moe_forward_norm(const void* x, int T, const int* ids, const float* weights, int topk,
+                                       const nvfp4b_moe_experts* ex, const void* norm_weight, float eps,
+                                       float in_gscale, float* out, int flags, void* workspace, void* stream) {
+    if (!norm_weight) return NVFP4B_ERR_NULL;
+    if (!aligned16(norm_weight)) return NVFP4B_ERR_ALIGN;
+    if (!(in_gscale > 0.0f) || !(eps >= 0.0f)) return NVFP4B_ERR_ARG;
+    return moe_forward(x, T, ids, weights, topk, ex, in_gscale, nullptr, out, flags, workspace,
+                       CombineNext{nullptr, nullptr}, stream, static_cast<const uint16_t*>(norm_weight), eps);
 }
 
 extern "C" int nvfp4b_moe_forward_chain(const void* x, int T, const int* ids, const float* weights, int topk,

@@ -197,6 +197,15 @@ int nvfp4b_moe_forward(const void* x, int T, const int* ids, const float* weight
                        const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
                        int flags, void* workspace, void* stream);
 
+/* nvfp4b_moe_forward with the MoE input's RMSNorm fused into the quantise-dispatch (the reference normalises the
+ * residual with pre_feedforward_layernorm_2 before its experts, src/forward.cu:535, kernels/elementwise.cu:10-22):
+ * each token row is x * rsqrt(mean(x^2) + eps) * norm_weight in fp32 (norm_weight bf16 [H], 16-byte aligned) and
+ * those fp32 values are quantised -- the normalised activations are never written.  Static activation global scale
+ * only (in_gscale > 0, e.g. the checkpoint's input_global_scale): a dynamic one would need the normalised amax first. */
+int nvfp4b_moe_forward_norm(const void* x, int T, const int* ids, const float* weights, int topk,
+                            const nvfp4b_moe_experts* experts, const void* norm_weight, float eps, float in_gscale,
+                            float* out, int flags, void* workspace, void* stream);
+
 /* nvfp4b_moe_forward for a stack of layers on a residual stream: the combine also writes each finished out row
  * rounded to bf16 (RNE) into x_next [T, H] and max |x_next| into *d_amax_next (zeroed by this call after the layer
  * has read its own inputs, so x_next/d_amax_next may be the layer's own x/d_in_amax).  That is the next layer's

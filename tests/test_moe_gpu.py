@@ -254,3 +254,43 @@ def test_cfg3_full_size_sampled_tokens():
     ok, msg = gate_w4a4(out.cpu().numpy()[tokens], y_ref[tokens])
     assert ok, msg
     assert rows_needed.size == 48 * topk
+
+
+def test_moe_forward_norm_fuses_input_rmsnorm():
+    """nvfp4b_moe_forward_norm: the MoE input RMSNorm (x * rsqrt(mean(x^2) + eps) * w, the reference's
+    pre_feedforward_layernorm_2) inside the quantise-dispatch.  The dispatched rows are the oracle quantisation of the
+    float32-normalised rows (the device sums the squares in another order, so a value may sit on the other side of a
+    rounding boundary in rare elements), and the layer matches the independent W4A4 oracle on the normalised input."""
+    p, P = make_problem(96, 512, 128, 32, 8, seed=73)
+    ids, w, _, g_h = route_and_calibrate(p, P)
+    rng = np.random.default_rng(5)
+    nw = orc.f32_to_bf16_bits((1.0 + 0.1 * rng.standard_normal(P["H"])).astype(np.float32))
+    x2 = orc.rmsnorm(orc.bf16_bits_to_f32(P["xb"]), orc.bf16_bits_to_f32(nw), eps=1e-6)
+    g_in = orc.global_scale_from_amax(np.float32(np.abs(x2).max()))
+    out = p.moe_forward_norm(P["x"], ids, w, P["arena"], P["ws"], bf16_to_dev(nw), float(g_in), eps=1e-6)
+    torch.cuda.synchronize()
+    assert p.read_device_error() == 0
+    ids_np, w_np = ids.cpu().numpy(), w.cpu().numpy()
+    v = p.moe_view(P["ws"], P["T"], P["H"], P["I"], P["E"], P["topk"])
+    ref = orc.moe_dispatch_ref(ids_np, P["E"])
+    rows = ref["m_tiles"] * 128
+    real = ref["row_token"] >= 0
+    pk, sf = native.quantize_f32(x2, g_in)
+    a_codes = orc.unpack_nibbles(v["a_codes"].cpu().numpy()[:rows][real])
+    a_sf = orc.unswizzle_scales(v["a_scales"].cpu().numpy(), v["rows"], P["H"])[:rows][real]
+    want_codes = orc.unpack_nibbles(pk[ref["row_token"][real]])
+    assert (a_codes == want_codes).mean() >= 0.999
+    assert (a_sf == sf[ref["row_token"][real]]).mean() >= 0.999
+    full, _ = orc.moe_w4a4_ref(x2, ids_np, w_np, P["experts"], g_in, g_h)
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.linalg.norm(got - full) / np.linalg.norm(full) <= 2e-2
+
+
+def test_moe_forward_norm_rejects_dynamic_scale():
+    p, P = make_problem(8, 256, 64, 4, 2, seed=79)
+    nw = bf16_to_dev(orc.f32_to_bf16_bits(np.ones(256, np.float32)))
+    ids = torch.zeros((8, 2), dtype=torch.int32, device="cuda")
+    ids[:, 1] = 1
+    w = torch.full((8, 2), 0.5, device="cuda")
+    with pytest.raises(p.NvFp4Error):
+        p.moe_forward_norm(P["x"], ids, w, P["arena"], P["ws"], nw, 0.0)
