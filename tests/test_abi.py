@@ -99,3 +99,29 @@ def test_linear_workspace_and_argument_errors_need_no_gpu(built):
     assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, 16, None, 1.0, 1.0, 2, 16, big, None) == -3      # W4A4: no tiles
     assert L.nvfp4b_linear(16, 16, 4, 4, 64, 16, None, 16, 1.0, 1.0, 1, 16, big, None) == -3      # W4A16: no raw
     assert L.nvfp4b_amax_f32(8, 16, 16, None) == -2
+
+
+def test_ep_p2p_layout_and_argument_errors_need_no_gpu(built):
+    pkg = load_package()
+    G, C, H = 8, 736, 2816
+    nbytes, off = pkg.ep_p2p_buffer_layout(G, C, H)
+    rb = pkg.ep_record_bytes(H)
+    assert rb == H // 2 + H // 16 + 16
+    assert all(o % 256 == 0 for o in off)
+    assert off[1] >= G * C * rb and off[2] - off[1] >= G * C * H * 2
+    assert off[3] - off[2] >= 4 * G and off[4] - off[3] >= 8 * G and nbytes - off[4] >= 16
+    L = pkg._p2p_sigs()
+    assert L.nvfp4b_ep_p2p_buffer_bytes(0, C, H, None) == 0
+    assert L.nvfp4b_ep_p2p_buffer_bytes(G, C, 100, None) == 0            # H % 256
+    peers = pkg.EpPeers()                                                 # all NULL
+    assert L.nvfp4b_ep_p2p_combine(4, H, 8, 128, 16, peers, 16, 0, None) == -3
+    peers = pkg.EpPeers(0, 0, C, 16, 16, 16, 16, 16, 16, 16, 16, 16)      # G = 0
+    assert L.nvfp4b_ep_p2p_combine(4, H, 8, 128, 16, peers, 16, 0, None) == -1
+    peers = pkg.EpPeers(2, 2, C, 16, 16, 16, 16, 16, 16, 16, 16, 16)      # rank >= G
+    assert L.nvfp4b_ep_p2p_combine(4, H, 8, 128, 16, peers, 16, 0, None) == -1
+    peers = pkg.EpPeers(0, 2, C, 16, 16, 16, 16, 16, 16, 16, 16, 16)
+    assert L.nvfp4b_ep_p2p_combine(4, H, 8, 128, 16, peers, 16, 4, None) == -7   # unknown flag
+    assert L.nvfp4b_ep_p2p_combine_chain(4, H, 8, 128, 16, peers, 16, 0, None, 16, None) == -3
+    Lm = pkg._moe_sigs()
+    assert Lm.nvfp4b_moe_forward_norm(16, 4, 16, 16, 8, None, None, 1e-6, 1.0, 16, 0, 16, None) == -3
+    assert Lm.nvfp4b_moe_forward_norm(16, 4, 16, 16, 8, None, 16, 1e-6, 0.0, 16, 0, 16, None) == -7
