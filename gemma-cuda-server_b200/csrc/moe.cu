@@ -618,6 +618,7 @@ struct DownEpi {
     unsigned* const* peer_flags = nullptr;
     unsigned* state = nullptr;
     int rank = 0, G = 0, capacity = 0;
+    bool transpose = false;     // rows through the shared-memory transpose (launched with DownTransposeCfg)
 
     // Padding rows of an expert segment (row_assign -1) produce nothing: a warp whose 32 rows are all padding skips
     // its work.
@@ -646,10 +647,11 @@ struct DownEpi {
     // DETERMINISTIC, rows to local memory: each lane converts its row's 32-column chunk to fp16 and stores it as four
     // 16-byte pieces (64 contiguous bytes of the row); no shared-memory transpose, so the epilogue's per-tile cost --
     // which bounds this short-K GEMM -- is a handful of instructions per chunk.
-    // DETERMINISTIC, rows to peer memory (peer_back): 16-byte pieces of 32 different rows per store instruction cost
-    // NVLink packets of half a 32-byte sector each, so there each warp first transposes its 32 x 32 chunk through
-    // shared memory (32 x 33 floats, the EPI_SMEM of DownPeerCfg) and every store instruction writes four whole
-    // 64-byte row segments.
+    // DETERMINISTIC with `transpose`: each warp first transposes its 32 x 32 chunk through shared memory (32 x 33
+    // floats, the EPI_SMEM of DownTransposeCfg) and every store instruction writes four whole 64-byte row segments.
+    // Used for rows to peer memory (16-byte pieces of 32 different rows per instruction cost NVLink packets of half a
+    // 32-byte sector each) and for large row counts (the row buffer then streams to DRAM, where scattered 16-byte
+    // pieces cost more than the transpose: 125 vs 105 us for 32768 rows of 2816).
     template <int CH>
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
                                             uint8_t* esm) const {
@@ -658,10 +660,11 @@ struct DownEpi {
         const int e = ti.expert;
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
-            if (peer_back) {
+            if (transpose) {
                 const int lane = threadIdx.x & 31;
-                uint16_t* rowp = a >= 0 ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
-                                        : nullptr;
+                uint16_t* rowp = a < 0 ? nullptr
+                                 : peer_back ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
+                                             : y + (long long)a * H;
                 float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 4) * (32 * 33);   // warps 4..
                 const int sub = lane >> 3, q = (lane & 7) * 4;
 #pragma unroll
@@ -989,7 +992,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back,
 
 using GroupCfg = KCfg<256, 4, 1, 8>;
 using DownCfg = KCfg<256, 4, 1, 8>;   // K = I is short: the epilogue bounds it (direct fp16 row stores)
-using DownPeerCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // rows to peer memory: + transpose tiles
+using DownTransposeCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // + the epilogue's transpose tiles
+constexpr int kDownTransposeRows = 16384;   // local row buffers at least this large take the transposed stores
 
 // ---------------------------------------------------------------------------------------------------------------
 // host orchestration
@@ -1104,9 +1108,10 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
             e.G = peers->G;
             e.capacity = peers->capacity;
         }
-        static_assert(DownPeerCfg::BM == DownCfg::BM && DownPeerCfg::BN == DownCfg::BN, "same tiles, same maps");
-        st = peers ? launch_core<DownPeerCfg>(ma, mb, cp, sc, e, sm_count(), s)
-                   : launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
+        e.transpose = peers != nullptr || (long long)T * topk >= kDownTransposeRows;
+        static_assert(DownTransposeCfg::BM == DownCfg::BM && DownTransposeCfg::BN == DownCfg::BN, "same tiles, maps");
+        st = e.transpose ? launch_core<DownTransposeCfg>(ma, mb, cp, sc, e, sm_count(), s)
+                         : launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
         if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
         if (next.x) {
             const cudaError_t err = cudaMemsetAsync(next.amax, 0, sizeof(float), s);
