@@ -364,12 +364,13 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         uint32_t aphase = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             const TileInfo ti = sched.tile(t);
+            // a warp whose 32 rows the epilogue policy marks dead (padding) neither loads nor processes them; the
+            // policy's row lookup is made before the wait so its latency stays off the accumulator hand-off
+            const bool work = col_base < ti.n_mma && __any_sync(0xFFFFFFFFu, epi.row_live(ti, row));
             if (!mbar_wait(&tfull[abuf], aphase, sflag, kErrTimeoutEpilogue)) break;
             tc_fence_after();
             const uint32_t addr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(abuf * C::BN + col_base);
             uint32_t r[C::CHUNKS][32];
-            // a warp whose 32 rows the epilogue policy marks dead (padding) neither loads nor processes them
-            const bool work = col_base < ti.n_mma && __any_sync(0xFFFFFFFFu, epi.row_live(ti, row));
             if (work) {
 #pragma unroll
                 for (int c = 0; c < C::CHUNKS; ++c) tmem_ld_32x32b_x32(addr + 32 * c, r[c]);
