@@ -812,6 +812,7 @@ def main():
         cpu = {"value": cv, "unit": W.unit, "cores": native.num_threads() if W.name == "quant" else cpu_cores(),
                "kind": "port", "sample": sample}
 
+    W.config["device_error"] = int(pkg.read_device_error())   # a bounded device wait that expired (0: none)
     if W.name == "ep":
         W.config["capacity_overflow"] = bool(sum(int(Ld["ops"].overflow.item()) for Ld in W.layers))
         W.config["graph"] = "one CUDA graph per step" if getattr(W, "graph", None) is not None else "eager"
