@@ -56,7 +56,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep"], default="ep")
+    ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep", "w4a16", "linear"], default="ep")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ep-exchange", choices=["auto", "p2p", "nccl", "local"], default="auto",
                     help="ep: records/rows stored over NVLink peer memory by the kernels (p2p), NCCL all-to-all "
@@ -268,6 +268,142 @@ class GemmWorkload:
             if el >= seconds:
                 break
         return 2.0 * rows * self.N * self.K * n / el / 1e12, f"{n} x ({rows} rows of cfg2 M x N={self.N} x K={self.K}) float64"
+
+
+class W4a16Workload:
+    """The reference's W4A16 decode path at its largest call (src/forward.cu:596, fp4_gemv on the lm_head): NVFP4
+    weights [N=262144, K=2816] (raw codes + e4m3 scales, 415 MB) times one fp16 activation row -> fp32 logits.  A
+    weight stream: the roofline is HBM."""
+    name = "w4a16"
+    unit = "GB/s"
+    dtype = "nvfp4 weights x fp16"
+
+    def __init__(self, pkg, torch, orc, M=1, N=262144, K=2816):
+        self.pkg, self.torch = pkg, torch
+        self.M, self.N, self.K = M, N, K
+        gen = torch.Generator(device="cuda").manual_seed(77)
+        self.wp = torch.randint(0, 256, (N, K // 2), generator=gen, dtype=torch.uint8, device="cuda")
+        self.ws = torch.randint(0x30, 0x40, (N, K // 16), generator=gen, dtype=torch.uint8, device="cuda")
+        self.wg = 2688.0 / 0.1
+        self.x = torch.randn((M, K), generator=gen, device="cuda").half()
+        self.out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        self.kernel_bytes = N * K // 2 + N * K // 16 + M * K * 2 + M * N * 4
+        self.units_per_step = self.kernel_bytes
+        self.launches_per_step = 1
+        self.config = {"workload": "W4A16 decode GEMV (fp4_gemv), lm_head shape", "M": M, "N": N, "K": K,
+                       "weights": "random NVFP4 codes and e4m3 scales (raw, unswizzled)",
+                       "l2": "flushed between steps (256 MiB write + 256 MiB read); weights 415 MB > L2"}
+
+    def step(self, mark=None):
+        if mark is not None:
+            mark("kernel")
+        self.pkg.w4a16_gemm(self.out, self.wp, self.ws, self.wg, self.x, self.M, self.N, self.K)
+        if mark is not None:
+            mark("kernel_end")
+
+    def value(self, seconds_per_step):
+        return self.units_per_step / seconds_per_step / 1e9
+
+    def e2e_setup(self):
+        t = self.torch
+        self.h_x = t.empty((self.M, self.K), dtype=t.float16, pin_memory=True)
+        self.h_x.copy_(self.x.cpu())
+        self.h_out = t.empty((self.M, self.N), dtype=t.float32, pin_memory=True)
+        self.d_x = t.empty_like(self.x)
+        return self.M * self.K * 2, self.M * self.N * 4
+
+    def e2e_step(self):
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        self.pkg.w4a16_gemm(self.out, self.wp, self.ws, self.wg, self.d_x, self.M, self.N, self.K)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_run(self, native, orc, seconds):
+        """Oracle port: dequantise a row sample of the weights (code * e4m3 / g) and multiply in float32 numpy."""
+        import numpy as np
+        rows = 8192
+        wp = self.wp[:rows].cpu().numpy()
+        ws = self.ws[:rows].cpu().numpy()
+        x = self.x.float().cpu().numpy()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            wd = orc.dequantize(wp, ws, self.wg).astype(np.float32)
+            x @ wd.T
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        b = rows * (self.K // 2 + self.K // 16)
+        return b * n / el / 1e9, f"{n} x {rows} weight rows of the lm_head shape (dequantise + matmul, numpy)"
+
+
+class LinearWorkload:
+    """The dense Linear wired to the W4A4 path (src/forward.cu:424-445 at prefill): fp32 [M=4096, K=2816] in ->
+    NVFP4 quantise (static activation scale) -> tcgen05 GEMM against NVFP4 W [N=2112, K] -> fp32 row-major out, one
+    nvfp4b_linear call (the MLP gate/up projection shape of the model)."""
+    name = "linear"
+    unit = "TFLOP/s"
+    dtype = "nvfp4"
+
+    def __init__(self, pkg, torch, orc, M=4096, N=2112, K=2816):
+        import numpy as np
+        self.pkg, self.torch = pkg, torch
+        self.M, self.N, self.K = M, N, K
+        gen = torch.Generator(device="cuda").manual_seed(78)
+        self.x = torch.randn((M, K), generator=gen, device="cuda")
+        w = (torch.randn((N, K), generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+        self.wg = float(orc.global_scale_from_amax(pkg.amax(w).item()))
+        self.wp, self.ws_tiled = pkg.quantize(w, gscale=self.wg)
+        self.ws_raw = torch.zeros((N, K // 16), dtype=torch.uint8, device="cuda")   # unused on the W4A4 path
+        self.ag = float(orc.global_scale_from_amax(self.x.abs().max().item()))
+        self.out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        self.ws = pkg.linear_workspace(M, K)
+        self.units_per_step = 2.0 * M * N * K
+        self.launches_per_step = 2      # quantise + GEMM
+        self.config = {"workload": "dense Linear, W4A4 prefill path (nvfp4b_linear)", "M": M, "N": N, "K": K,
+                       "activation_scale": "static", "out": "fp32 row-major",
+                       "l2": "flushed between steps (256 MiB write + 256 MiB read)"}
+
+    def step(self, mark=None):
+        if mark is not None:
+            mark("kernel")
+        self.pkg.linear(self.out, self.x, self.wp, self.ws_raw, self.ws_tiled, self.wg, a_gscale=self.ag,
+                        mode=self.pkg.LINEAR_W4A4, workspace=self.ws)
+        if mark is not None:
+            mark("kernel_end")
+
+    def value(self, seconds_per_step):
+        return self.units_per_step / seconds_per_step / 1e12
+
+    def e2e_setup(self):
+        t = self.torch
+        self.h_x = t.empty((self.M, self.K), dtype=t.float32, pin_memory=True)
+        self.h_x.copy_(self.x.cpu())
+        self.h_out = t.empty((self.M, self.N), dtype=t.float32, pin_memory=True)
+        self.d_x = t.empty_like(self.x)
+        return self.M * self.K * 4, self.M * self.N * 4
+
+    def e2e_step(self):
+        self.d_x.copy_(self.h_x, non_blocking=True)
+        self.pkg.linear(self.out, self.d_x, self.wp, self.ws_raw, self.ws_tiled, self.wg, a_gscale=self.ag,
+                        mode=self.pkg.LINEAR_W4A4, workspace=self.ws)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def cpu_run(self, native, orc, seconds):
+        """Oracle port: quantise a row sample of x (C port), dequantise, float64 matmul against the dequantised W."""
+        import numpy as np
+        rows = 64
+        x = self.x[:rows].cpu().numpy()
+        wd = orc.dequantize(self.wp.cpu().numpy(), orc.unswizzle_scales(self.ws_tiled.cpu().numpy(), self.N, self.K),
+                            self.wg)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            px, sx = native.quantize_f32(x, self.ag)
+            orc.dequantize(px, sx, self.ag) @ wd.T
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return 2.0 * rows * self.N * self.K * n / el / 1e12, f"{n} x ({rows} rows of M x N={self.N} x K={self.K})"
 
 
 class MoeWorkload:
@@ -659,7 +795,8 @@ def main():
             raise SystemExit("--ep-exchange local needs one GPU")
         W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange)
     else:
-        W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload}[args.workload](pkg, torch, orc)
+        W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload, "w4a16": W4a16Workload,
+             "linear": LinearWorkload}[args.workload](pkg, torch, orc)
     # L2 flush between steps: write a 256 MiB buffer (evicts the step's data), then read another 256 MiB buffer so
     # the L2 is left holding clean lines (otherwise the next step would pay the flush's own write-backs).
     flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -786,6 +923,18 @@ def main():
                 "kernel": "nvf4_gemm_kernel<GroupedSched, GateUpEpi> (grouped gate/up, GELU + NVFP4 requant)",
                 "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
                 "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
+    elif W.name == "w4a16":
+        achieved = W.kernel_bytes / kern_s / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "w4a16_fast_kernel",
+                "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
+    elif W.name == "linear":
+        achieved = W.units_per_step / kern_s / 1e12
+        fp4_peak = peaks["bf16_tflops"] * 4.0
+        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
+                "frac": achieved / fp4_peak, "traffic": None,
+                "kernel": "nvfp4b_linear (quantize_kernel<float> + nvf4_gemm_pair_kernel, fp32 row-major out)",
+                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4"}
     elif W.name == "ep":
         n_recv = W.received(len(W.layers) - 1)     # records this rank's experts ran (last layer of the last step)
         achieved = 2.0 * n_recv * 3 * W.I * W.H / kern_s / 1e12
