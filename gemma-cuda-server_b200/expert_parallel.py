@@ -29,6 +29,14 @@ import torch
 import torch.distributed as dist
 
 
+def default_capacity(T_cap: int, topk: int, G: int) -> int:
+    """Record slots per (source, destination) pair: the even share n = T_cap * topk / G plus 8 sqrt(n) + 32 (eight
+    standard deviations of a uniform router's count), rounded up to 16, at most T_cap * topk (which cannot
+    overflow)."""
+    share = T_cap * topk / G
+    return min(T_cap * topk, int(share + 8 * share ** 0.5 + 32 + 15) // 16 * 16)
+
+
 class KernelOps:
     """Device side of one expert-parallel layer on this rank: buffers sized for up to T_cap tokens per rank and
     `capacity` records per (source, destination) pair.  The all-to-alls move every slot, so the default is the even
@@ -45,8 +53,7 @@ class KernelOps:
         H, I = experts.H, experts.I
         self.H = H
         if capacity is None:
-            share = T_cap * topk / G
-            capacity = min(T_cap * topk, int(share + 8 * share ** 0.5 + 32 + 15) // 16 * 16)
+            capacity = default_capacity(T_cap, topk, G)
         self.capacity = capacity
         self.record_bytes = pkg.ep_record_bytes(H)
         n = G * capacity
@@ -153,11 +160,7 @@ class P2PKernelOps:
         self.exp_ws = pkg.moe_workspace(G * self.capacity, experts.H, experts.I, E // G, 1, device=device)
         self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
 
-    @staticmethod
-    def default_capacity(T_cap: int, topk: int, G: int) -> int:
-        """Even share n = T_cap * topk / G plus 8 sqrt(n) + 32, at most T_cap * topk (which cannot overflow)."""
-        share = T_cap * topk / G
-        return min(T_cap * topk, int(share + 8 * share ** 0.5 + 32 + 15) // 16 * 16)
+    default_capacity = staticmethod(default_capacity)
 
     def dispatch(self, x, ids, weights, in_gscale=None, in_amax=None):
         T = x.shape[0]
