@@ -8,7 +8,10 @@ Two layers:
 * the reference's operator API under its own names and argument order (include/nvfp4_quant.h:10-11,
   include/fp4_gemm.h:13-35 of the reference): ``nvfp4_quantize_activations``, ``nvfp4_scale_buffer_bytes``,
   ``nvfp4_swizzle_scales``, ``nvfp4_gemm``, ``w4a16_gemm``, ``fp4_gemv`` -- device pointers as torch tensors;
-* tensor-level helpers used by the tests and the benchmark: ``quantize``, ``amax``, ``gemm``.
+* tensor-level helpers used by the tests and the benchmark: ``quantize``, ``amax``, ``gemm``, ``linear``, the MoE
+  layer (``moe_route``, ``moe_forward`` with its chained and fused-norm forms, ``MoeExperts``), and the
+  expert-parallel entry points (``ep_*`` over NCCL slots, ``ep_p2p_*`` over peer memory with the ``ipc_*`` set-up
+  helpers; ``expert_parallel.py`` orchestrates them).
 """
 from __future__ import annotations
 
