@@ -133,7 +133,8 @@ class PeerExchange:
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (call once every rank is done with them)."""
-        torch.cuda.synchronize()
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
         for p in self._opened:
             self.pkg.ipc_close(p)
         for p in self._owned:
