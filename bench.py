@@ -4,10 +4,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ep|quant|gemm|moe] [--impl ours|reference]
 
 Workloads (synthetic seeded inputs and random-init weights with the configs' shapes):
-  ep (default)  cfg4: expert-parallel MoE stack on the N GPUs -- 30 MoE layers shaped as cfg3, 512 rows per GPU per
-                step, the 128 experts sharded 128/N per GPU, records and returned rows exchanged with NCCL
-                all-to-alls per layer; the step is replayed from one CUDA graph.  Metric tokens/s over all GPUs
-                (weak scaling: 512 rows per GPU at every N).
+  ep (default)  cfg4: expert-parallel MoE stack on the N GPUs -- 30 MoE layers shaped as cfg3, 512 rows (32 sequences
+                x 16 draft tokens) per step in total, split 512/N per GPU (strong scaling; --ep-scaling weak keeps
+                512 rows per GPU), the 128 experts sharded 128/N per GPU, records and returned rows stored into the
+                other GPUs' memory over NVLink by the kernels (one GPU runs the single-GPU layer); the step is
+                replayed from one CUDA graph.  Metric tokens/s over all GPUs.  At N = 1 the line also carries the
+                driver-visible sub-results `quant` (cfg1 T=8192) and `gemm` (cfg2 M=8192, K=4096, N=14336), timed in
+                the same process under the same rules.
   quant         cfg1 at its largest size: bf16 [8192, 2816] ~ N(0,1) with 0.1% x50 outliers.  One step = device
                 global amax + NVFP4 quantise (codes, tile-layout e4m3 scales, fp32 amax).  Metric GB/s of
                 algorithmic bytes T*K*(2 + 1/2 + 1/16) + 4.
@@ -25,8 +28,9 @@ from pinned host memory with the host->device copy of the inputs and the device-
 the timed region.
 
 --impl reference times the reference's CPU implementation on the same config (rank 0 only): the quantiser (the
-oracle's C port of scripts/nvfp4_ref.py:71-82, all host threads) for quant, the MoE experts() semantics of
-scripts/ref_forward.py:160-192 (numpy, all host threads) for moe and ep.
+oracle's C port of scripts/nvfp4_ref.py:71-82, all host threads) for quant, the float64 dequant-matmul
+(scripts/nvfp4_ref.py:102) on a row sample for gemm, the MoE experts() semantics of scripts/ref_forward.py:160-192
+(numpy, all host threads, experts dequantised before timing) for moe and ep.
 """
 from __future__ import annotations
 
@@ -58,6 +62,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep", "w4a16", "linear"], default="ep")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ep-rows", type=int, default=512, help="ep: rows per step (512 = 32 sequences x 16 drafts)")
+    ap.add_argument("--ep-scaling", choices=["strong", "weak"], default="strong",
+                    help="ep: strong = --ep-rows in total, split over the GPUs (the cfg4 contract); weak = --ep-rows "
+                         "per GPU")
+    ap.add_argument("--no-sub", action="store_true", help="ep at N=1: skip the quant and gemm sub-results")
     ap.add_argument("--ep-exchange", choices=["auto", "p2p", "nccl", "local"], default="auto",
                     help="ep: records/rows stored over NVLink peer memory by the kernels (p2p), NCCL all-to-all "
                          "(nccl), the single-GPU MoE layer (local, 1 GPU only), or auto = p2p on 2+ GPUs, local on 1")
@@ -147,9 +156,10 @@ class QuantWorkload:
         self.amax = torch.empty(1, dtype=torch.float32, device="cuda")
         self.packed = torch.empty((T, K // 2), dtype=torch.uint8, device="cuda")
         self.scales = torch.empty(pkg.nvfp4_scale_buffer_bytes(T, K), dtype=torch.uint8, device="cuda")
-        self.units_per_step = T * K * 2.5625 + 4          # algorithmic bytes (SURVEY cfg1)
+        self.units_per_step = T * K * 2.5625 + 4          # algorithmic bytes: bf16 in, codes, scales, amax
         self.kernel_bytes = T * K * 2.5625                 # the quantise kernel alone (input read + outputs)
         self.launches_per_step = 2
+        self.kernel_name = "quantize_bf16_rows_kernel"
         self.config = {"workload": "cfg1 activation quantiser, dynamic global scale", "T": T, "K": K,
                        "input": "bf16 N(0,1), 0.1% entries x50", "l2": "flushed between steps (256 MiB write + 256 MiB read)"}
 
@@ -221,6 +231,7 @@ class GemmWorkload:
         self.units_per_step = 2.0 * M * N * K
         self.kernel_bytes = None
         self.launches_per_step = 1
+        self.kernel_name = "nvf4_gemm_pair_kernel (256x256 tiles on a CTA pair, tcgen05 cta_group::2)"
         self.config = {"workload": "cfg2 dense prefill GEMM, largest config", "M": M, "N": N, "K": K,
                        "out": "bf16 row-major, alpha fused", "l2": "flushed between steps (256 MiB write + 256 MiB read)"}
 
@@ -290,6 +301,7 @@ class W4a16Workload:
         self.kernel_bytes = N * K // 2 + N * K // 16 + M * K * 2 + M * N * 4
         self.units_per_step = self.kernel_bytes
         self.launches_per_step = 1
+        self.kernel_name = "w4a16_gemv_kernel" if M == 1 else "w4a16_fast_kernel"
         self.config = {"workload": "W4A16 decode GEMV (fp4_gemv), lm_head shape", "M": M, "N": N, "K": K,
                        "weights": "random NVFP4 codes and e4m3 scales (raw, unswizzled)",
                        "l2": "flushed between steps (256 MiB write + 256 MiB read); weights 415 MB > L2"}
@@ -359,6 +371,7 @@ class LinearWorkload:
         self.ws = pkg.linear_workspace(M, K)
         self.units_per_step = 2.0 * M * N * K
         self.launches_per_step = 2      # quantise + GEMM
+        self.kernel_name = "nvfp4b_linear (quantize_kernel<float> + nvf4_gemm_pair_kernel, fp32 row-major out)"
         self.config = {"workload": "dense Linear, W4A4 prefill path (nvfp4b_linear)", "M": M, "N": N, "K": K,
                        "activation_scale": "static", "out": "fp32 row-major",
                        "l2": "flushed between steps (256 MiB write + 256 MiB read)"}
@@ -446,6 +459,7 @@ class MoeWorkload:
         self.kernel_flops = 2.0 * T * topk * (2 * I) * H          # grouped gate/up GEMM, routed rows only
         self.step_flops = 2.0 * T * topk * 3 * I * H + 2.0 * T * E * H
         self.launches_per_step = 12   # amax, router GEMM + top-k, hist/plan/rank/pad/scatter, gate/up, down, combine
+        self.kernel_name = "nvf4_gemm_kernel<GroupedSched, GateUpEpi> (grouped gate/up, GELU + NVFP4 requant)"
         self.config = {"workload": "cfg3 MoE FFN layer", "tokens": T, "hidden": H, "experts": E, "inter": I,
                        "topk": topk, "router": "bf16 [128, 2816], softmax-top8-renorm",
                        "scales": "x: dynamic global (device amax); h: static per-expert (calibrated once)",
@@ -483,47 +497,50 @@ class MoeWorkload:
         self.h_out.copy_(self.out, non_blocking=True)
 
     def cpu_run(self, native, orc, seconds):
-        """The reference's experts() semantics (scripts/ref_forward.py:175-192: dequantise each needed expert,
-        per-token loop) in W4A4 on a token sample, numpy float32."""
+        """The reference's experts() semantics (scripts/ref_forward.py:175-192: per-token loop over the selected
+        experts, gelu_tanh(gate) * up, down, weighted sum) in W4A4 on a token sample, numpy float32 on all host
+        threads.  The sample's experts are dequantised BEFORE the timer (as the reference's experts() works on
+        weights loaded once); the timed part is the per-token work: quantise x, the expert matmuls, requantise h."""
         import numpy as np
         S = 16
         ids = self.ids[:S].cpu().numpy()
         w = self.wts[:S].cpu().numpy()
         x = self.x[:S].float().cpu().numpy()
         gin = orc.global_scale_from_amax(self.in_amax.item())
-        w13 = {}
-        t0 = time.perf_counter()
-        _, _, xd = orc.quantize_rows(x.astype(np.float64), gin)
-        xd = xd.astype(np.float32)
-        out = np.zeros((S, self.H), np.float32)
         a2 = self.arena.a2_gscale.cpu().numpy()
-        for t in range(S):
-            for j in range(self.topk):
-                e = int(ids[t, j])
-                if e not in w13:
-                    g = float(self.arena.w1_gscale[e].item())
-                    pk = self.arena.w13[e].cpu().numpy()
-                    sf = orc.unswizzle_scales(self.arena.w13_scales[e].cpu().numpy(), 2 * self.I, self.H)
-                    pd = self.arena.w2[e].cpu().numpy()
-                    sd = orc.unswizzle_scales(self.arena.w2_scales[e].cpu().numpy(), self.H, self.I)
-                    w13[e] = (orc.dequantize(pk, sf, g).astype(np.float32),
-                              orc.dequantize(pd, sd, float(self.arena.w2_gscale[e].item())).astype(np.float32))
-                wgu, wd = w13[e]
-                y = wgu @ xd[t]
-                h = orc.gelu_tanh(y.reshape(-1, 2, 16)[:, 0].reshape(-1)) * y.reshape(-1, 2, 16)[:, 1].reshape(-1)
-                _, _, hd = orc.quantize_rows(h[None].astype(np.float64), a2[e])
-                out[t] += w[t, j] * (wd @ hd[0].astype(np.float32))
-            if time.perf_counter() - t0 > seconds and t >= 1:
-                S = t + 1
+        mats = {}
+        for e in sorted(set(int(v) for v in ids.reshape(-1))):
+            g = float(self.arena.w1_gscale[e].item())
+            sf = orc.unswizzle_scales(self.arena.w13_scales[e].cpu().numpy(), 2 * self.I, self.H)
+            sd = orc.unswizzle_scales(self.arena.w2_scales[e].cpu().numpy(), self.H, self.I)
+            mats[e] = (native.dequantize(self.arena.w13[e].cpu().numpy(), sf, g).astype(np.float32),
+                       native.dequantize(self.arena.w2[e].cpu().numpy(), sd,
+                                         float(self.arena.w2_gscale[e].item())).astype(np.float32))
+        n, t0 = 0, time.perf_counter()
+        while True:
+            _, _, xd = orc.quantize_rows(x.astype(np.float64), gin)
+            xd = xd.astype(np.float32)
+            out = np.zeros((S, self.H), np.float32)
+            for t in range(S):
+                for j in range(self.topk):
+                    e = int(ids[t, j])
+                    wgu, wd = mats[e]
+                    y = wgu @ xd[t]
+                    h = orc.gelu_tanh(y.reshape(-1, 2, 16)[:, 0].reshape(-1)) * y.reshape(-1, 2, 16)[:, 1].reshape(-1)
+                    _, _, hd = orc.quantize_rows(h[None].astype(np.float64), a2[e])
+                    out[t] += w[t, j] * (wd @ hd[0].astype(np.float32))
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
                 break
-        el = time.perf_counter() - t0
-        return S / el, f"{S} tokens of cfg3 through the W4A4 experts() path (dequantised experts, float32)"
+        return S * n / el, (f"{n} x {S} tokens of cfg3 through the W4A4 experts() path (experts dequantised before "
+                            f"timing, float32)")
 
 
 class EpWorkload:
     """cfg4: expert-parallel decode/verify stack on G GPUs -- 30 stacked MoE FFN layers shaped as cfg3 (H=2816,
-    128 experts of I=704, top-8), 512 rows (32 sequences x 16 draft tokens) per rank per step, experts sharded
-    128/G per GPU.  Exchange per layer: routed records and returned rows stored into the other ranks' memory over
+    128 experts of I=704, top-8), experts sharded 128/G per GPU, T rows per rank per step: 512/G of the 32 sequences
+    x 16 draft tokens = 512 rows in total (scaling "strong", the cfg4 contract), or 512 per rank ("weak").  Exchange per layer: routed records and returned rows stored into the other ranks' memory over
     NVLink by the kernels (p2p, default on 2+ GPUs), or NCCL all-to-all (nccl); one GPU runs the single-GPU layer
     (local).  Layers are chained through an fp32 residual stream: each layer adds its MoE output, and its combine
     also leaves the next layer's bf16 input and amax."""
@@ -532,11 +549,12 @@ class EpWorkload:
     dtype = "nvfp4"
 
     def __init__(self, pkg, torch, orc, rank=0, world=1, group=None, T=512, H=2816, I=704, E=128, topk=8, L=30,
-                 exchange="p2p"):
+                 exchange="p2p", scaling="strong"):
         import numpy as np
         import gemma_cuda_server_b200.expert_parallel as epm
         self.pkg, self.torch = pkg, torch
         self.exchange = exchange
+        self.scaling = scaling
         self.ex = None
         if exchange == "p2p":       # one set of exchange buffers serves every layer (per-layer epochs)
             C = epm.P2PKernelOps.default_capacity(T, topk, world)
@@ -544,8 +562,13 @@ class EpWorkload:
                        else epm.PeerExchange.local_group(pkg, 1, C, H)[0])
         self.T, self.H, self.I, self.E, self.topk, self.L, self.G = T, H, I, E, topk, L, world
         El = E // world
-        gen = torch.Generator(device="cuda").manual_seed(4000 + rank)
-        self.x0 = torch.randn((T, H), generator=gen, device="cuda").to(torch.bfloat16)
+        if scaling == "strong":      # this rank's slice of the one 512-row batch (the same rows at every G)
+            gen = torch.Generator(device="cuda").manual_seed(4000)
+            self.x0 = torch.randn((T * world, H), generator=gen, device="cuda")[rank * T:(rank + 1) * T]
+            self.x0 = self.x0.to(torch.bfloat16).contiguous()
+        else:
+            gen = torch.Generator(device="cuda").manual_seed(4000 + rank)
+            self.x0 = torch.randn((T, H), generator=gen, device="cuda").to(torch.bfloat16)
         self.x = torch.empty_like(self.x0)
         self.res = torch.empty((T, H), dtype=torch.float32, device="cuda")
         self.amax = torch.zeros(1, dtype=torch.float32, device="cuda")
@@ -590,14 +613,21 @@ class EpWorkload:
         torch.cuda.synchronize()
         del cal_ws
         self.units_per_step = T                                   # rows of this rank; value() scales by G
+        self.kernel_name = ("one MoE layer (dispatch with fused quantiser, grouped gate/up and down GEMMs, combine)"
+                            if exchange == "local" else
+                            "expert side of one layer (record scatter, grouped gate/up and down GEMMs, rows stored "
+                            "back), including its wait for the other ranks' records")
+        self.traffic_key = "ep" if exchange == "local" else None
         # one amax, then per layer: router x2 + dispatch x4, expert x8, combine with the next input fused (p2p); the
         # single-GPU layer's hist/plan/rank/pad/quant-scatter, gate/up, down, combine (local); + the amax of the
         # next input (nccl, where the combine has no fused output)
         self.launches_per_step = {"local": 10, "p2p": 15, "nccl": 16}[exchange] * L + 1
         self.kernel_flops = 2.0 * T * topk * 3 * I * H            # expert GEMMs of one layer at even routing
         self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
-        self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_per_gpu": T, "hidden": H,
+        self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_total": T * world,
+                       "rows_per_gpu": T, "scaling": scaling, "hidden": H,
                        "experts": E, "experts_per_gpu": El, "inter": I, "topk": topk,
+                       "capacity": self.ex.capacity if self.ex is not None else None,
                        "exchange": ("NVFP4 records and fp16 rows stored to peer memory over NVLink by the pack kernel "
                                     "and the down-GEMM epilogue, per-layer flags (no collective)") if exchange == "p2p"
                        else ("none: one GPU holds every expert (single-GPU MoE layer)" if exchange == "local"
@@ -632,6 +662,39 @@ class EpWorkload:
         else:
             self.step()
         self.h_out.copy_(self.res, non_blocking=True)
+
+    def _expert_bytes(self):
+        I, H, p = self.I, self.H, self.pkg
+        return (2 * I * H // 2 + p.nvfp4_scale_buffer_bytes(2 * I, H)) + (H * I // 2 + p.nvfp4_scale_buffer_bytes(H, I))
+
+    def _rows_per_expert(self):
+        """Rows each local expert ran in the last layer of the last step (host read of the dispatch plan)."""
+        Ld = self.layers[-1]
+        ops = Ld["ops"]
+        El = self.E // self.G
+        if self.exchange == "local":
+            v = self.pkg.moe_view(ops.src_ws, self.T, self.H, self.I, El, self.topk)
+        else:
+            v = self.pkg.moe_view(ops.exp_ws, self.G * ops.capacity, self.H, self.I, El, 1)
+        return v["seg_count"].cpu().tolist()
+
+    def layer_bytes(self):
+        """Algorithmic DRAM bytes of the timed part of one layer: the NVFP4 weights (codes + tile scales) of every
+        local expert that received a row, read once, plus the layer's activations -- local layer: x in (bf16),
+        the residual read and written (fp32) and the next input out (bf16); expert side of a rank: the records in
+        (one per assignment) and one fp16 row per record out."""
+        counts = self._rows_per_expert()
+        hit = sum(1 for c in counts if c > 0)
+        n = sum(counts)
+        w = hit * self._expert_bytes()
+        if self.exchange == "local":
+            act = self.T * self.H * (2 + 4 + 4 + 2)
+        else:
+            act = n * (self.pkg.ep_record_bytes(self.H) + 2 * self.H)
+        return {"weights": w, "activations": act, "total": w + act, "experts_hit": hit, "rows": n}
+
+    def layer_flops(self):
+        return 2.0 * sum(self._rows_per_expert()) * 3 * self.I * self.H
 
     def received(self, li=0):
         """Records this rank's experts ran in layer li's last run."""
@@ -731,8 +794,42 @@ def run_reference_moe(args, world, orc):
         "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
+def run_reference_gemm(args, world, orc):
+    """The reference's CPU GEMM (scripts/nvfp4_ref.py:102, gen_fp4_gemm_testcase.py:60): float64 X_deq @ W_deq^T of
+    the NVFP4 operands, on cfg2's largest point (M=8192, K=4096, N=14336).  W is quantised and dequantised before
+    timing; each step multiplies a sample of 64 activation rows (quantise + dequantise + matmul, BLAS threads)."""
+    import numpy as np
+    import native
+    M, N, K, rows = 8192, 14336, 4096, 64
+    wb = orc.synth_bf16((N, K), 0.02, seed=12)
+    gw = orc.global_scale_from_amax(native.amax_bf16(wb))
+    wd = native.dequantize(*native.quantize_bf16(wb, gw), gw)
+    del wb
+    xb = orc.synth_bf16((rows * (args.warmup + args.steps), K), 1.0, seed=11)
+    gx = orc.global_scale_from_amax(native.amax_bf16(xb))
+
+    def step(i):
+        px, sx = native.quantize_bf16(xb[i * rows:(i + 1) * rows], gx)
+        return native.dequantize(px, sx, gx) @ wd.T
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.warmup, args.warmup + args.steps):
+        step(i)
+    el = time.perf_counter() - t0
+    val = 2.0 * rows * N * K * args.steps / el / 1e12
+    sample = f"{rows} of {M} rows per step, float64 dequant-matmul (N={N}, K={K})"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "cfg2 dense prefill GEMM, largest config", "M": M, "N": N, "K": K},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port", "sample": sample},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU quantiser (oracle C port, all host threads); rank 0 only."""
+    """--impl reference: the reference's CPU implementation of the workload's path on the host cores; rank 0 only."""
     if rank != 0:
         return
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -740,6 +837,9 @@ def run_reference(args, rank, world):
     import nvfp4_oracle as orc
     if args.workload in ("moe", "ep"):
         run_reference_moe(args, world, orc)
+        return
+    if args.workload == "gemm":
+        run_reference_gemm(args, world, orc)
         return
     if args.workload != "quant":
         print(json.dumps({"impl": "reference", "unavailable": "reference CPU arm is timed for the quant and MoE workloads"}))
@@ -764,6 +864,34 @@ def run_reference(args, rank, world):
         "cpu_baseline": {"value": val, "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{rows} of {T} rows per step (C port of scripts/nvfp4_ref.py:71-82)"},
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def roofline_of(W, kern_s, peaks, peak_src, steps_s=None):
+    """Roofline object of workload W's dominant kernel (or, for ep, one layer), from its event-timed duration."""
+    hbm = peaks["hbm_gbs"]
+    fp4_peak = peaks["bf16_tflops"] * 4.0
+    fp4_src = f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4"
+    if W.name in ("quant", "w4a16"):
+        achieved = W.kernel_bytes / kern_s / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": NCU_TRAFFIC.get(W.name), "kernel": W.kernel_name,
+                "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
+    if W.name == "ep":
+        b = W.layer_bytes()
+        achieved = b["total"] / kern_s / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": NCU_TRAFFIC.get(W.traffic_key), "kernel": W.kernel_name,
+                "algorithmic_bytes": b, "layer_us": kern_s * 1e6,
+                "tensor": {"achieved": W.layer_flops() / kern_s / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
+                           "frac": W.layer_flops() / kern_s / 1e12 / fp4_peak},
+                "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
+    flops = W.kernel_flops if W.name == "moe" else W.units_per_step
+    achieved = flops / kern_s / 1e12
+    roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s", "frac": achieved / fp4_peak,
+            "traffic": NCU_TRAFFIC.get(W.name), "kernel": W.kernel_name, "peak_source": fp4_src}
+    if W.name == "moe" and steps_s:
+        roof["step_tflops"] = W.step_flops / steps_s / 1e12
+    return roof
 
 
 def main():
@@ -793,7 +921,10 @@ def main():
         exchange = args.ep_exchange if args.ep_exchange != "auto" else ("p2p" if world > 1 else "local")
         if exchange == "local" and world > 1:
             raise SystemExit("--ep-exchange local needs one GPU")
-        W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange)
+        if args.ep_scaling == "strong" and args.ep_rows % world:
+            raise SystemExit(f"--ep-rows {args.ep_rows} does not split over {world} GPUs")
+        rows = args.ep_rows // world if args.ep_scaling == "strong" else args.ep_rows
+        W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange, T=rows, scaling=args.ep_scaling)
     else:
         W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload, "w4a16": W4a16Workload,
              "linear": LinearWorkload}[args.workload](pkg, torch, orc)
@@ -802,11 +933,9 @@ def main():
     flush_w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     flush_r = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
 
-    class _Flush:
-        def zero_(self):
-            flush_w.zero_()
-            flush_r.sum()
-    flush = _Flush()
+    def flush():
+        flush_w.zero_()
+        flush_r.sum()
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -814,32 +943,40 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    props = torch.cuda.get_device_properties(local)
-    uuid = getattr(props, "uuid", None)
-    uuid = ("GPU-" + str(uuid)) if uuid is not None and not str(uuid).startswith("GPU-") else uuid
-    sampler = ClockSampler(local, uuid)
+    def eager_marks(Wk, n):
+        """Kernel marks ("kernel" / "kernel_end" events on the launching stream) from n eager steps."""
+        marks = [{} for _ in range(n)]
+        for i in range(n):
+            flush()
 
-    with sampler:
-        for _ in range(args.warmup):
-            flush.zero_()
-            W.step()
+            def mark(name, i=i):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                marks[i][name] = ev
+            Wk.step(mark)
         barrier()
-        # The expert-parallel stack (30 layers of ~16 small launches and 3 collectives) is launch-bound at 512 rows:
-        # capture one step in a CUDA graph (fixed-size buffers, no host reads inside) and replay it.
+        return [m["kernel"].elapsed_time(m["kernel_end"]) for m in marks]
+
+    def time_steps(Wk, steps, warmup, graph_capture, profiler_range=False):
+        """W untimed warm-up steps, then `steps` timed steps (CUDA events on the launching stream around each, L2
+        flushed before each outside the events).  Returns (step ms list, kernel ms list, graph or None)."""
+        for _ in range(warmup):
+            flush()
+            Wk.step()
+        barrier()
         graph = None
-        if W.name == "ep":
+        if graph_capture:     # a launch-bound stack: one CUDA graph per step (fixed buffers, no host reads inside)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                W.step()
+                Wk.step()
             barrier()
-            W.graph = graph
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        marks = [{} for _ in range(args.steps)]
-        if args.cuda_profiler_range:
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        marks = [{} for _ in range(steps)]
+        if profiler_range:
             torch.cuda.profiler.start()
-        for i in range(args.steps):
-            flush.zero_()
+        for i in range(steps):
+            flush()
             starts[i].record(stream)
 
             def mark(name, i=i):
@@ -849,31 +986,33 @@ def main():
             if graph is not None:
                 graph.replay()
             else:
-                W.step(mark)
+                Wk.step(mark)
             stops[i].record(stream)
         barrier()
-        if args.cuda_profiler_range:
+        if profiler_range:
             torch.cuda.profiler.stop()
-        step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
-        if graph is not None:          # kernel marks from eager steps (events cannot be taken inside the replay)
-            marks = [{} for _ in range(3)]
-            for i in range(3):
-                flush.zero_()
+        step_ms = [a.elapsed_time(b) for a, b in zip(starts, stops)]
+        if graph is not None:          # events cannot be taken inside a graph replay: marks from eager steps
+            kern_ms = eager_marks(Wk, 3)
+        else:
+            kern_ms = [m["kernel"].elapsed_time(m["kernel_end"]) for m in marks]
+        return step_ms, kern_ms, graph
 
-                def mark(name, i=i):
-                    ev = torch.cuda.Event(enable_timing=True)
-                    ev.record(stream)
-                    marks[i][name] = ev
-                W.step(mark)
-            barrier()
-        kern_ms = [m["kernel"].elapsed_time(m["kernel_end"]) for m in marks]
+    props = torch.cuda.get_device_properties(local)
+    uuid = getattr(props, "uuid", None)
+    uuid = ("GPU-" + str(uuid)) if uuid is not None and not str(uuid).startswith("GPU-") else uuid
+    sampler = ClockSampler(local, uuid)
+
+    with sampler:
+        step_ms, kern_ms, graph = time_steps(W, args.steps, args.warmup, W.name == "ep", args.cuda_profiler_range)
+        W.graph = graph
         # sustained window for the clock record (same steps, untimed); a step count all ranks agree on
         per_step = torch.tensor([sum(step_ms) / len(step_ms)], dtype=torch.float64, device="cuda")
         if world > 1:
             dist.all_reduce(per_step, op=dist.ReduceOp.MAX)
         n_clock = max(1, min(2000, int(args.clock_seconds * 1e3 / max(float(per_step.item()), 1e-3))))
         for i in range(n_clock):
-            flush.zero_()
+            flush()
             if graph is not None:
                 graph.replay()
             else:
@@ -910,49 +1049,22 @@ def main():
 
     peaks, peak_src = load_peaks()
     kern_s = statistics.mean(kern_ms) / 1e3
-    if W.name == "quant":
-        achieved = W.kernel_bytes / kern_s / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC["quant"],
-                "kernel": "quantize_bf16_rows_kernel", "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
-    elif W.name == "moe":
-        achieved = W.kernel_flops / kern_s / 1e12
-        fp4_peak = peaks["bf16_tflops"] * 4.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": achieved / fp4_peak, "traffic": NCU_TRAFFIC.get("moe"),
-                "kernel": "nvf4_gemm_kernel<GroupedSched, GateUpEpi> (grouped gate/up, GELU + NVFP4 requant)",
-                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
-                "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
-    elif W.name == "w4a16":
-        achieved = W.kernel_bytes / kern_s / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "w4a16_fast_kernel",
-                "peak_source": f"{peak_src} hbm_gbs (copy, burst)"}
-    elif W.name == "linear":
-        achieved = W.units_per_step / kern_s / 1e12
-        fp4_peak = peaks["bf16_tflops"] * 4.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": achieved / fp4_peak, "traffic": None,
-                "kernel": "nvfp4b_linear (quantize_kernel<float> + nvf4_gemm_pair_kernel, fp32 row-major out)",
-                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4"}
-    elif W.name == "ep":
-        n_recv = W.received(len(W.layers) - 1)     # records this rank's experts ran (last layer of the last step)
-        achieved = 2.0 * n_recv * 3 * W.I * W.H / kern_s / 1e12
-        fp4_peak = peaks["bf16_tflops"] * 4.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": achieved / fp4_peak, "traffic": None,
-                "kernel": ("one MoE layer (dispatch with fused quantiser, grouped gate/up and down GEMMs, combine)"
-                           if W.exchange == "local" else
-                           "expert side of one layer (record scatter, grouped gate/up and down GEMMs)"),
-                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4",
-                "step_tflops": W.step_flops * args.steps / (sum(step_ms) / 1e3) / 1e12}
-    else:
-        achieved = W.units_per_step / kern_s / 1e12
-        fp4_peak = peaks["bf16_tflops"] * 4.0
-        roof = {"bound": "tensor", "achieved": achieved, "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": achieved / fp4_peak, "traffic": NCU_TRAFFIC["gemm"],
-                "kernel": "nvf4_gemm_pair_kernel (256x256 tiles on a CTA pair, tcgen05 cta_group::2)",
-                "peak_source": f"{peak_src} bf16_tflops (burst) x 4 = dense FP4 rate of kind::mxf4nvf4"}
+    roof = roofline_of(W, kern_s, peaks, peak_src, steps_s=sum(step_ms) / 1e3 / args.steps)
+
+    # driver-visible sub-results at N = 1: the quantiser (cfg1) and the dense GEMM (cfg2), same timing rules
+    sub = None
+    if W.name == "ep" and world == 1 and not args.no_sub:
+        sub = {}
+        sub_steps = max(10, min(args.steps, 50))
+        for Wk in (QuantWorkload(pkg, torch, orc), GemmWorkload(pkg, torch, orc)):
+            s_ms, k_ms, _ = time_steps(Wk, sub_steps, max(3, args.warmup), False)
+            ks = statistics.mean(k_ms) / 1e3
+            r = roofline_of(Wk, ks, peaks, peak_src)
+            sub[Wk.name] = {"value": Wk.value(sum(s_ms) / len(s_ms) / 1e3), "unit": Wk.unit,
+                            "ms_per_step": sum(s_ms) / len(s_ms), "steps": sub_steps, "config": Wk.config,
+                            "roofline": r}
+            del Wk
+        torch.cuda.synchronize()
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
@@ -968,14 +1080,18 @@ def main():
     if world > 1:
         dist.barrier()
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": METRIC, "value": value, "unit": W.unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": getattr(W, "scaling", "weak"),
             "vs_baseline": None, "dtype": W.dtype, "data": "synthetic (seeded, shapes of BASELINE.json configs)",
             "config": {**W.config, "parallelism": f"expert parallel x{world}" if W.name == "ep" else f"replicas x{world}"},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": W.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": W.launches_per_step * args.steps, "clocks": clocks}))
+            "gpu_launches": W.launches_per_step * args.steps, "clocks": clocks}
+        if sub is not None:
+            line["sub_results"] = sub
+        print(json.dumps(line))
     if getattr(W, "graph", None) is not None:      # a graph holding NCCL calls must go before the process group
         W.graph = None
         graph = None

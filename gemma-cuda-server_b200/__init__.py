@@ -533,6 +533,7 @@ def _p2p_sigs():
                                    ctypes.c_int, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_combine_chain": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, PP, _P,
                                          ctypes.c_int, _P, _P, _P], ctypes.c_int),
+        "nvfp4b_ep_set_peer_wait_ns": ([ctypes.c_ulonglong], ctypes.c_int),
         "nvfp4b_ep_p2p_state": ([PP, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_recv_counts": ([PP, _P], ctypes.c_int),
         "nvfp4b_ipc_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
@@ -556,6 +557,15 @@ def ep_p2p_buffer_layout(G: int, capacity: int, H: int):
     if n == 0:
         raise NvFp4Error("ep_p2p_buffer_bytes", -1)
     return n, [int(v) for v in off]
+
+
+def ep_set_peer_wait_ns(ns: int) -> None:
+    """Bound (nanoseconds, per flag) of the waits on other ranks' flags in kernels launched from now on; 0 restores
+    the default of 10 s.  A wait that runs out records device error 4 (read_device_error) instead of hanging."""
+    _check("ep_set_peer_wait_ns", _p2p_sigs().nvfp4b_ep_set_peer_wait_ns(int(ns)))
+
+
+PEER_TIMEOUT = 4      # device error code of an expired wait on another rank's flag
 
 
 def ep_p2p_state(peers: EpPeers) -> list[int]:

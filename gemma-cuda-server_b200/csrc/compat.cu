@@ -8,11 +8,26 @@
 #include "nvfp4_b200.h"
 #include "nvfp4_quant.h"
 
+// The reference's void entry points report failure only through the CUDA error state, which its callers read with
+// cudaGetLastError() / CU() (src/forward.cu:23).  An argument error (K not a multiple of 16, a null or misaligned
+// pointer) is rejected by the C ABI before anything is launched, so on its own it would leave that state clean and
+// the caller would go on with unwritten buffers.  compat_fail() therefore leaves a launch error behind: a launch
+// with an empty grid, which the runtime rejects on the host with cudaErrorInvalidConfiguration -- nothing reaches
+// the device, and the next cudaGetLastError() returns (and clears) it.
+namespace {
+__global__ void compat_failed_call_kernel() {}
+}  // namespace
+
+static void compat_fail(const char* fn, int status, cudaStream_t stream) {
+    fprintf(stderr, "%s: nvfp4_b200 status %d\n", fn, status);
+    compat_failed_call_kernel<<<0, 1, 0, stream>>>();
+}
+
 // include/nvfp4_quant.h:10-11 -- static global scale, fp32 input; void, errors via the CUDA error state.
 void nvfp4_quantize_activations(const float* dX, uint8_t* dPacked, uint8_t* dScalesSwz, int M, int K, float gscale,
                                 cudaStream_t stream) {
     const int st = nvfp4b_quantize_f32(dX, M, K, gscale, nullptr, dPacked, dScalesSwz, stream);
-    if (st != NVFP4B_OK) fprintf(stderr, "nvfp4_quantize_activations: error %d (M=%d K=%d)\n", st, M, K);
+    if (st != NVFP4B_OK) compat_fail("nvfp4_quantize_activations", st, stream);
 }
 
 // include/fp4_gemm.h:13 (kernels/fp4_gemm.cu:14-19)
@@ -35,14 +50,14 @@ extern "C" int nvfp4b_w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* w
 void w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16, int M, int N,
                 int K, cudaStream_t s) {
     const int st = nvfp4b_w4a16_gemm(out, wp, ws, w_gscale, x16, M, N, K, s);
-    if (st != NVFP4B_OK) fprintf(stderr, "w4a16_gemm: error %d (M=%d N=%d K=%d)\n", st, M, N, K);
+    if (st != NVFP4B_OK) compat_fail("w4a16_gemm", st, s);
 }
 
 // include/fp4_gemm.h:26-27
 void fp4_gemv(float* y, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16, int N, int K,
               cudaStream_t s) {
     const int st = nvfp4b_w4a16_gemm(y, wp, ws, w_gscale, x16, 1, N, K, s);
-    if (st != NVFP4B_OK) fprintf(stderr, "fp4_gemv: error %d (N=%d K=%d)\n", st, N, K);
+    if (st != NVFP4B_OK) compat_fail("fp4_gemv", st, s);
 }
 
 // include/fp4_gemm.h:31-35 -- fp32 column-major D (ld = M); lt / workspace unused.  0 on success.

@@ -12,6 +12,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "gemm.cuh"
 #include "gemm_core.cuh"
@@ -145,7 +147,7 @@ using Tile256 = KCfg<256, 4, 1, 8>;
 using Tile128 = KCfg<128, 6, 2, 4>;
 using TilePair = PairCfg<5, 8, 8 * kStoreTileBytes>;   // + bf16 store staging tiles
 
-int g_variant = 0;   // 0 = automatic, 1 = TILE_256, 2 = TILE_128, 3 = TILE_PAIR
+std::atomic<int> g_variant{0};   // 0 = automatic, 1 = TILE_256, 2 = TILE_128, 3 = TILE_PAIR
 
 template <class C, int OUT>
 int run_dense(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const uint8_t* b_sf, const GemmParams& p,
@@ -247,7 +249,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn enc = nullptr;
+    static std::atomic<EncodeTiledFn> cached{nullptr};   // host threads may race to fill it (same value)
+    EncodeTiledFn enc = cached.load(std::memory_order_acquire);
     if (!enc) {
         void* ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
@@ -255,6 +258,7 @@ static EncodeTiledFn encode_fn() {
             q != cudaDriverEntryPointSuccess)
             return nullptr;
         enc = reinterpret_cast<EncodeTiledFn>(ptr);
+        cached.store(enc, std::memory_order_release);
     }
     return enc;
 }
@@ -289,7 +293,8 @@ int gemm_dense(const uint8_t* a, const uint8_t* a_sf, const uint8_t* b, const ui
                cudaStream_t stream) {
     // Automatic: the CTA-pair tiles whenever there are more rows than one 128-row block (they halve each SM's
     // operand traffic and stage the output through shared memory); 128 x 256 single-CTA tiles otherwise.
-    const int v = g_variant != 0 ? g_variant : (p.M > 128 ? 3 : 1);
+    const int sel = g_variant.load(std::memory_order_relaxed);
+    const int v = sel != 0 ? sel : (p.M > 128 ? 3 : 1);
     if (v == 3) return dispatch_pair(a, a_sf, b, b_sf, p, stream);
     if (v == 2) return dispatch_out<Tile128>(a, a_sf, b, b_sf, p, stream);
     return dispatch_out<Tile256>(a, a_sf, b, b_sf, p, stream);

@@ -25,6 +25,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -663,18 +665,19 @@ int pair_clusters_resident() {
 template <class C, class Sched, class Epi>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& msfa, const CUtensorMap& msfb,
                 const CoreParams& cp, const Sched& s, const Epi& e, int tiles, cudaStream_t stream) {
-    static int clusters[64] = {0};
+    static std::atomic<int> clusters[64];     // per device; host threads may race to fill it (same value)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NVFP4B_ERR_CUDA;
-    if (clusters[dev] == 0) {
+    int resident = clusters[dev].load(std::memory_order_acquire);
+    if (resident == 0) {
         cudaError_t err = cudaFuncSetAttribute(nvf4_gemm_pair_kernel<C, Sched, Epi>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
         if (err != cudaSuccess) return record_cuda_error(err);
-        const int n = pair_clusters_resident<C, Sched, Epi>();
-        if (n <= 0) return record_cuda_error(cudaErrorLaunchOutOfResources);
-        clusters[dev] = n;
+        resident = pair_clusters_resident<C, Sched, Epi>();
+        if (resident <= 0) return record_cuda_error(cudaErrorLaunchOutOfResources);
+        clusters[dev].store(resident, std::memory_order_release);
     }
-    const int n = tiles < clusters[dev] ? tiles : clusters[dev];
+    const int n = tiles < resident ? tiles : resident;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -695,14 +698,14 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
 template <class C, class Sched, class Epi>
 int launch_core(const CUtensorMap& ma, const CUtensorMap& mb, const CoreParams& cp, const Sched& s, const Epi& e,
                 int grid, cudaStream_t stream) {
-    static bool attr_done[64] = {false};
+    static std::atomic<bool> attr_done[64];   // per device; host threads may race to set it (idempotent)
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
         cudaError_t err = cudaFuncSetAttribute(nvf4_gemm_kernel<C, Sched, Epi>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
         if (err != cudaSuccess) return record_cuda_error(err);
-        attr_done[dev] = true;
+        if (dev >= 0 && dev < 64) attr_done[dev].store(true, std::memory_order_release);
     }
     nvf4_gemm_kernel<C, Sched, Epi><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, cp, s, e);
     return launch_status();

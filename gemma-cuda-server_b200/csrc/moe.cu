@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -440,7 +441,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-constexpr unsigned long long kPeerWaitNs = 10000000000ull;   // 10 s per flag, then the wait gives up
+// Bound of every wait on another rank's flag: 10 s by default, settable with nvfp4b_ep_set_peer_wait_ns (read on
+// the host when a kernel that waits is launched, and passed to it as an argument).
+constexpr unsigned long long kPeerWaitDefaultNs = 10000000000ull;
+std::atomic<unsigned long long> g_peer_wait_ns{kPeerWaitDefaultNs};
 
 // Per-rank private words (nvfp4b_ep_peers::state): the epoch of the current layer (advanced by the last block of
 // the layer's pack kernel, which publishes the layer's records with it), and the completion counters of the two
@@ -477,10 +481,11 @@ __device__ __forceinline__ bool last_block_arrived(unsigned* counter) {
     return s_last != 0u;
 }
 
-// Thread 0 of a block: waits until flags[g] >= epoch for every g < G (acquire, system scope; bounded, a timeout is
-// recorded in *err and the wait ends, and once *err is set no later wait spins at all); the block barrier then
-// makes what the flags publish visible to the block.
-__device__ __forceinline__ void wait_peer_flags(const unsigned* flags, int G, unsigned epoch, int* err) {
+// Thread 0 of a block: waits until flags[g] >= epoch for every g < G (acquire, system scope; bounded by wait_ns
+// per flag, after which kErrTimeoutPeer is recorded in *err and the wait ends, and once *err is set no later wait
+// spins at all); the block barrier then makes what the flags publish visible to the block.
+__device__ __forceinline__ void wait_peer_flags(const unsigned* flags, int G, unsigned epoch, int* err,
+                                                unsigned long long wait_ns) {
     if (threadIdx.x == 0) {
         bool ok = true;
         const volatile int* verr = err;
@@ -488,7 +493,7 @@ __device__ __forceinline__ void wait_peer_flags(const unsigned* flags, int G, un
             if ((int)(ld_acquire_sys(flags + g) - epoch) >= 0) continue;
             const unsigned long long t0 = sm100::globaltimer();
             while ((int)(ld_acquire_sys(flags + g) - epoch) < 0) {
-                if (*verr != 0 || sm100::globaltimer() - t0 > kPeerWaitNs) { ok = false; break; }
+                if (*verr != 0 || sm100::globaltimer() - t0 > wait_ns) { ok = false; break; }
                 __nanosleep(64);
             }
         }
@@ -920,8 +925,9 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
 __global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* records, int n, int H, int capacity,
                                                       const int* recv_counts, int* __restrict__ ids,
                                                       float* __restrict__ w, const unsigned* wait_flags, int G,
-                                                      const unsigned* state, int* err) {
-    if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err);
+                                                      const unsigned* state, int* err,
+                                                      unsigned long long wait_ns) {
+    if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err, wait_ns);
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     if (i % capacity >= recv_counts[i / capacity]) {
@@ -961,8 +967,9 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
 __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back, int T, int H, int topk,
                                                          const int* __restrict__ slot, float* __restrict__ out,
                                                          int accumulate, const unsigned* wait_flags, int G,
-                                                         const unsigned* state, int* err, const CombineNext next) {
-    if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err);
+                                                         const unsigned* state, int* err,
+                                                         unsigned long long wait_ns, const CombineNext next) {
+    if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err, wait_ns);
     const int chunks = H >> 3;
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool valid = idx < (long long)T * chunks;
@@ -1185,7 +1192,8 @@ int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_count
     if (!err) return NVFP4B_ERR_CUDA;
     ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, capacity, recv_counts, w.ep_ids, w.ep_w,
                                                    peers ? peers->my_flags : nullptr, G,
-                                                   peers ? peers->state : nullptr, err);
+                                                   peers ? peers->state : nullptr, err,
+                                                   g_peer_wait_ns.load(std::memory_order_relaxed));
     moe_hist_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist);
     moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
                                       w.tile_expert);
@@ -1549,7 +1557,7 @@ extern "C" int nvfp4b_ep_combine(const uint16_t* y_back, int T, int H, int topk,
     const Workspace w = carve(const_cast<void*>(workspace), T, H, 32, E, topk);
     const long long threads = (long long)T * (H / 8);
     ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, nullptr, 0, nullptr, nullptr,
+        y_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, nullptr, 0, nullptr, nullptr, 0ull,
         CombineNext{nullptr, nullptr});
     return launch_status();
 }
@@ -1633,7 +1641,7 @@ static int ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, 
     const long long threads = (long long)T * (H / 8);
     ep_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
         peers->my_back, T, H, topk, w.ep_ids, out, (flags & NVFP4B_MOE_ACCUMULATE) ? 1 : 0, peers->my_flags + peers->G,
-        peers->G, peers->state, err, next);
+        peers->G, peers->state, err, g_peer_wait_ns.load(std::memory_order_relaxed), next);
     return launch_status();
 }
 
@@ -1648,6 +1656,13 @@ extern "C" int nvfp4b_ep_p2p_combine_chain(int T, int H, int topk, int E, const 
     if (!x_next || !d_amax_next) return NVFP4B_ERR_NULL;
     return ep_p2p_combine(T, H, topk, E, workspace, peers, out, flags,
                           CombineNext{static_cast<uint16_t*>(x_next), d_amax_next}, stream);
+}
+
+extern "C" int nvfp4b_ep_set_peer_wait_ns(unsigned long long ns) {
+    if (ns == 0) ns = kPeerWaitDefaultNs;
+    if (ns < 1000ull || ns > 600000000000ull) return NVFP4B_ERR_ARG;
+    g_peer_wait_ns.store(ns, std::memory_order_relaxed);
+    return NVFP4B_OK;
 }
 
 extern "C" int nvfp4b_ep_p2p_state(const nvfp4b_ep_peers* peers, unsigned* host_words4) {

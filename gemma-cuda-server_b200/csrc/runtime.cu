@@ -1,6 +1,8 @@
 // runtime.cu -- library-wide host helpers: error bookkeeping, device properties, sizes.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace nvfp4b {
@@ -10,17 +12,21 @@ static thread_local int t_last_cuda_error = 0;
 // Kernels whose bounded waits expire record a code here (through the pointer they are given).
 __device__ int g_device_error = 0;
 
+// The per-device caches below may be filled by several host threads at once (each computes the same value), so
+// their entries are atomics.
 int* device_error_ptr() {
-    static int* cached[64] = {nullptr};
+    static std::atomic<int*> cached[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!cached[dev]) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_device_error);
+    int* p = cached[dev].load(std::memory_order_acquire);
+    if (!p) {
+        void* q = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&q, g_device_error);
         if (e != cudaSuccess) { record_cuda_error(e); return nullptr; }
-        cached[dev] = static_cast<int*>(p);
+        p = static_cast<int*>(q);
+        cached[dev].store(p, std::memory_order_release);
     }
-    return cached[dev];
+    return p;
 }
 
 int record_cuda_error(cudaError_t e) {
@@ -29,15 +35,15 @@ int record_cuda_error(cudaError_t e) {
 }
 
 int sm_count() {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (cached[dev] == 0) {
-        int n = 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cached[dev] = n;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 }  // namespace nvfp4b

@@ -37,6 +37,13 @@ def default_capacity(T_cap: int, topk: int, G: int) -> int:
     return min(T_cap * topk, int(share + 8 * share ** 0.5 + 32 + 15) // 16 * 16)
 
 
+def no_drop_capacity(T_cap: int, topk: int, G: int) -> int:
+    """Record slots per (source, destination) pair that can never overflow: every assignment of T_cap tokens.  On the
+    peer-memory path only the records that exist cross the link, so this costs memory only: G * T_cap * topk *
+    (record + fp16 row) bytes per rank (237 MB at G = 8, 512 tokens, top-8, H = 2816)."""
+    return T_cap * topk
+
+
 class KernelOps:
     """Device side of one expert-parallel layer on this rank: buffers sized for up to T_cap tokens per rank and
     `capacity` records per (source, destination) pair.  The all-to-alls move every slot, so the default is the even
@@ -109,12 +116,24 @@ class PeerExchange:
         """This process's exchange in a group of G processes, one per GPU of the node: allocates, shares the CUDA
         IPC handle with every rank (all_gather_object over `group`) and maps the others' buffers."""
         rank = dist.get_rank(group)
+        if dist.get_world_size(group) != G:
+            raise ValueError(f"exchange for {G} ranks created in a group of {dist.get_world_size(group)}")
         nbytes, _ = pkg.ep_p2p_buffer_layout(G, capacity, H)
         base = pkg.ipc_alloc(nbytes)
-        handles = [None] * G
-        dist.all_gather_object(handles, pkg.ipc_handle(base), group=group)
+        # Every rank publishes its handle with the layout it was built for: a rank that disagrees on G, capacity or
+        # H would store records and rows at offsets the others do not read, so a mismatch stops every rank here.
+        mine = (pkg.ipc_handle(base), G, capacity, H)
+        got = [None] * G
+        try:
+            dist.all_gather_object(got, mine, group=group)
+            layouts = {(g, c, h) for _, g, c, h in got}
+            if len(layouts) != 1:
+                raise ValueError(f"ranks disagree on the exchange layout (G, capacity, H): {sorted(layouts)}")
+        except BaseException:
+            pkg.ipc_free(base)
+            raise
         bases, opened = [], []
-        for r, h in enumerate(handles):
+        for r, (h, *_) in enumerate(got):
             if r == rank:
                 bases.append(base)
             else:
@@ -161,7 +180,9 @@ class P2PKernelOps:
         self.exp_ws = pkg.moe_workspace(G * self.capacity, experts.H, experts.I, E // G, 1, device=device)
         self.overflow = torch.zeros(1, dtype=torch.int32, device=device)
 
-    default_capacity = staticmethod(default_capacity)
+    # Skewed routing (real routers are far from uniform) must not drop tokens, and padding never crosses the link
+    # here, so the peer-memory path defaults to the capacity that cannot overflow.
+    default_capacity = staticmethod(no_drop_capacity)
 
     def dispatch(self, x, ids, weights, in_gscale=None, in_amax=None):
         T = x.shape[0]

@@ -352,6 +352,13 @@ int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, 
 int nvfp4b_ep_p2p_combine_chain(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
                                 float* out, int flags, void* x_next, float* d_amax_next, void* stream);
 
+/* Bound of every wait on another rank's flag (records landed, rows landed) in kernels launched after this call:
+ * ns nanoseconds per flag, 1 us ... 600 s; 0 restores the default of 10 s.  A wait that runs out records
+ * NVFP4B_ERR_TIMEOUT's device code (nvfp4b_read_device_error() == 4) and its kernel goes on; the exchange's layer
+ * epochs are then out of step between the ranks, so the exchange buffers must be created anew before the next
+ * layer.  A CUDA graph keeps the bound its kernels were captured with.  Host-side setting, no CUDA call. */
+int nvfp4b_ep_set_peer_wait_ns(unsigned long long ns);
+
 /* Debug reads (synchronous, not for capture): a rank's private words (layer epoch, completion counters, spare) and
  * its receive counts [G] (records from each source in the last layer). */
 int nvfp4b_ep_p2p_state(const nvfp4b_ep_peers* peers, unsigned* host_words4);

@@ -31,6 +31,7 @@ def lib():
         _c.orc_amax_bf16.restype = ctypes.c_float
         _c.orc_swizzle_scales.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int]
         _c.orc_num_threads.restype = ctypes.c_int
+        _c.orc_dequantize_rows.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_float, _P]
     return _c
 
 
@@ -51,6 +52,17 @@ def quantize_f32(x: np.ndarray, gscale) -> tuple[np.ndarray, np.ndarray]:
     sf = np.empty((m, k // 16), np.uint8)
     lib().orc_quantize_rows_f32(_ptr(x), m, k, float(np.float32(gscale)), _ptr(packed), _ptr(sf))
     return packed, sf
+
+
+def dequantize(packed: np.ndarray, sf_logical: np.ndarray, gscale) -> np.ndarray:
+    """float64 [rows, K] = e2m1(code) * (e4m3(scale) / gscale); same values as nvfp4_oracle.dequantize, threaded."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    sf_logical = np.ascontiguousarray(sf_logical, dtype=np.uint8)
+    rows, k = packed.shape[0], packed.shape[1] * 2
+    assert sf_logical.shape == (rows, k // 16)
+    out = np.empty((rows, k), np.float64)
+    lib().orc_dequantize_rows(_ptr(packed), _ptr(sf_logical), rows, k, float(np.float32(gscale)), _ptr(out))
+    return out
 
 
 def amax_bf16(bits: np.ndarray) -> np.float32:

@@ -154,3 +154,27 @@ int orc_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Dequantise NVFP4 rows in float64: out[r, k] = e2m1(code) * (e4m3(scale) / gscale), the value order of
+ * nvfp4_oracle.dequantize (scripts/ref_forward.py:51-64, dequant_linear).  packed [rows, K/2] (even element in the
+ * low nibble), sf_logical [rows, K/16]. */
+void orc_dequantize_rows(const uint8_t* packed, const uint8_t* sf_logical, int rows, int K, float gscale,
+                         double* out) {
+    static const double k_e2m1[16] = {0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6};
+    const double g = (double)gscale;
+    const int kb = K / 16;
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* pr = packed + (size_t)r * (K / 2);
+        const uint8_t* sr = sf_logical + (size_t)r * kb;
+        double* orow = out + (size_t)r * K;
+        for (int b = 0; b < kb; ++b) {
+            const double s = e4m3_value(sr[b]) / g;
+            for (int i = 0; i < 8; ++i) {
+                const uint8_t v = pr[b * 8 + i];
+                orow[b * 16 + 2 * i] = k_e2m1[v & 15] * s;
+                orow[b * 16 + 2 * i + 1] = k_e2m1[v >> 4] * s;
+            }
+        }
+    }
+}

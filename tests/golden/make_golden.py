@@ -1,9 +1,9 @@
 """Generate the golden vectors under tests/golden/ by running the REFERENCE's own Python functions.
 
-Run it in a checkout where the reference project is available (path in $NVFP4_REFERENCE_ROOT, default
-``/root/reference``)::
+Run it where the reference project is available, giving its checkout as the argument (or in
+$NVFP4_REFERENCE_ROOT)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference checkout>
 
 The reference modules open a model checkpoint at import time, so they cannot be imported; instead the needed
 function definitions are extracted with ``ast`` and executed in a fresh namespace:
@@ -28,7 +28,10 @@ import sys
 import numpy as np
 
 HERE = pathlib.Path(__file__).resolve().parent
-REF = pathlib.Path(os.environ.get("NVFP4_REFERENCE_ROOT", "/root/reference"))
+_REF_ARG = next((a for a in sys.argv[1:] if not a.startswith("-")), None) or os.environ.get("NVFP4_REFERENCE_ROOT")
+if not _REF_ARG:
+    raise SystemExit("usage: make_golden.py <reference checkout>  (or set NVFP4_REFERENCE_ROOT)")
+REF = pathlib.Path(_REF_ARG)
 sys.path.insert(0, str(HERE.parent.parent / "oracle"))
 import nvfp4_oracle as orc  # noqa: E402  (only for seeded input generation helpers)
 

@@ -27,6 +27,12 @@ def test_reference_arm_quant_line():
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
-def test_reference_arm_unavailable_workload():
+def test_reference_arm_gemm_line():
     d = _run("--impl", "reference", "--workload", "gemm", "--steps", "3", "--warmup", "3")
+    assert d["impl"] == "reference" and d["unit"] == "TFLOP/s" and d["value"] > 0
+    assert d["config"]["M"] == 8192 and d["config"]["N"] == 14336 and d["config"]["K"] == 4096
+
+
+def test_reference_arm_unavailable_workload():
+    d = _run("--impl", "reference", "--workload", "w4a16", "--steps", "3", "--warmup", "3")
     assert d["impl"] == "reference" and "unavailable" in d

@@ -88,3 +88,66 @@ def test_peer_exchange_tables_gloo():
         assert mine == (r, G, C, own + off[0], own + off[1], own + off[2], own + off[3], own + off[4])
         assert freed == [own]
         assert closed == [(1 << 40) * (r + 1) + g * (1 << 30) for g in range(G) if g != r]
+
+
+# ---- failures of the set-up, made on the host: a layout mismatch, a rank that never joins --------------------------
+
+def _fault_worker(rank, world, port, mode, q):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    try:
+        pkg = load_package()
+        import gemma_cuda_server_b200.expert_parallel as epm
+        fake = FakeIpc(pkg, rank)
+        if mode == "absent" and rank == 1:
+            time.sleep(12)                     # joined the process group, never posts its exchange handle
+            q.put((rank, "absent", 0.0, fake.freed))
+            return
+        cap = C + 16 if (mode == "mismatch" and rank == 1) else C
+        t0 = time.monotonic()
+        try:
+            epm.PeerExchange.create(fake, world, cap, H, device="cpu")
+            outcome = "created"
+        except ValueError as e:
+            outcome = "ValueError: " + str(e)
+        except RuntimeError as e:              # gloo collective timeout / peer gone
+            outcome = "RuntimeError"
+        q.put((rank, outcome, time.monotonic() - t0, fake.freed))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run_fault(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_worker, args=(r, G, port, mode, q)) for r in range(G)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return {r: rest for r, *rest in (q.get(timeout=5) for _ in range(G))}
+
+
+def test_peer_exchange_layout_mismatch_stops_every_rank():
+    """One rank built for another capacity: every rank raises before mapping anything, and frees its allocation."""
+    res = _run_fault("mismatch")
+    for r, (outcome, _, freed) in res.items():
+        assert outcome.startswith("ValueError") and "disagree" in outcome, (r, outcome)
+        assert freed == [(1 << 30) * (r + 1)]
+
+
+def test_peer_exchange_absent_rank_times_out():
+    """A rank that never posts its handle: the other rank's set-up ends with an error within the process group's
+    timeout (3 s here) instead of waiting for ever, and frees its allocation."""
+    res = _run_fault("absent")
+    outcome, elapsed, freed = res[0]
+    assert outcome == "RuntimeError", outcome
+    assert elapsed < 10.0, elapsed
+    assert freed == [1 << 30]

@@ -210,3 +210,47 @@ def test_ep_p2p_combine_chain_outputs():
     finally:
         for e in ex:
             e.close()
+
+
+def test_ep_p2p_missing_rank_ends_in_timeout_not_hang():
+    """A rank that never dispatches (G = 2 emulated, rank 1 absent): rank 0's expert side waits for rank 1's records
+    and its combine for rank 1's rows.  With the peer-wait bound set to 50 ms the first wait runs out, the device
+    error word reads the peer-timeout code, the later wait does not spin at all, and the stream completes.  The
+    epochs of that exchange are then out of step, so a new exchange is made; it runs clean and bit-identical."""
+    import time
+    import gemma_cuda_server_b200.expert_parallel as epm
+    G, T = 2, 64
+    p, P = make_problem(T * G, 512, 128, 32, 8, seed=61)
+    P["ids"], P["w"], _, _ = route_and_calibrate(p, P)
+    E, k, H = P["E"], P["topk"], P["H"]
+    assert p.read_device_error() == 0
+    p.ep_set_peer_wait_ns(50_000_000)
+    ex = epm.PeerExchange.local_group(p, G, epm.P2PKernelOps.default_capacity(T, k, G), H)
+    try:
+        ops = [epm.P2PKernelOps(p, P["arena"].slice(r * E // G, (r + 1) * E // G), E, k, T, ex[r]) for r in range(G)]
+        x0 = P["x"][:T].contiguous()
+        amax0 = p.amax(x0)
+        torch.cuda.synchronize()
+        t0 = time.monotonic()
+        ops[0].dispatch(x0, P["ids"][:T].contiguous(), P["w"][:T].contiguous(), in_amax=amax0)
+        ops[0].expert()                                   # rank 1's records never land
+        out = torch.zeros((T, H), device="cuda")
+        ops[0].combine(out, False)                        # nor do rank 1's rows
+        torch.cuda.synchronize()
+        elapsed = time.monotonic() - t0
+        assert p.read_device_error(reset=True) == p.PEER_TIMEOUT
+        assert elapsed < 5.0, elapsed                     # one 50 ms wait, not 10 s per flag per block
+        assert torch.isfinite(out).all()                  # the kernels went on with what had landed
+    finally:
+        p.ep_set_peer_wait_ns(0)
+        for e in ex:
+            e.close()
+    assert p.read_device_error() == 0
+    ex, ops, xs, ids, ws, amaxes, outs = _emulate_p2p(p, P, G, T)
+    try:
+        assert p.read_device_error() == 0
+        for r in range(G):
+            assert torch.equal(outs[r], _ref(p, P, xs[r], ids[r], ws[r], amaxes[r]))
+    finally:
+        for e in ex:
+            e.close()

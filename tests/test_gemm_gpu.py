@@ -131,3 +131,53 @@ def test_gemm_matches_reference_cublaslt_when_built():
         pytest.skip(f"reference cuBLASLt nvfp4_gemm returned {rc} on this box")
     ok, msg = gate_fp4_gemm(D_ours.cpu().numpy(), D_ref.cpu().numpy())
     assert ok, msg
+
+
+# ---- cfg2 at full size: every (M, K, N) point of the dense prefill sweep ------------------------------------------
+
+_CFG2_SHAPES = [(M, K, N) for M in (128, 1024, 4096, 8192) for (K, N) in ((2816, 2816), (2816, 8448), (4096, 14336))]
+# every shape with the automatic tile choice, and with the other kernel family (the CTA-pair 256x256 kernel is the
+# automatic choice above 128 rows, the single-CTA 128x256 kernel at 128 rows)
+_CFG2_CASES = [(M, K, N, cfg) for (M, K, N) in _CFG2_SHAPES for cfg in (0, 3 if M <= 128 else 1)]
+_cfg2_cache = {}
+
+
+def _cfg2_operands(p, M, K, N):
+    """Full-size NVFP4 operands of one cfg2 point (quantised on the device, bit-exact to the oracle) and the float64
+    dequant-matmul of 66 rows (the first, the last and 64 sampled ones); one shape cached at a time."""
+    key = (M, K, N)
+    if key not in _cfg2_cache:
+        _cfg2_cache.clear()
+        xb = orc.synth_bf16((M, K), 1.0, seed=M + K)
+        wb = orc.synth_bf16((N, K), 0.02, seed=N + K + 1)
+        gx = orc.global_scale_from_amax(native.amax_bf16(xb))
+        gw = orc.global_scale_from_amax(native.amax_bf16(wb))
+        xq, xs = p.quantize(bf16_to_dev(xb), gscale=float(gx))
+        wq, ws = p.quantize(bf16_to_dev(wb), gscale=float(gw))
+        rng = np.random.default_rng(M * 7 + N)
+        rows = np.concatenate([[0], np.sort(rng.choice(np.arange(1, M - 1), 64, replace=False)), [M - 1]])
+        px, sx = native.quantize_bf16(xb[rows], gx)
+        pw, sw = native.quantize_bf16(wb, gw)
+        ref = native.dequantize(px, sx, gx) @ native.dequantize(pw, sw, gw).T
+        torch.cuda.synchronize()
+        _cfg2_cache[key] = (xq, xs, gx, wq, ws, gw, rows, ref)
+    return _cfg2_cache[key]
+
+
+@pytest.mark.parametrize("M,K,N,cfg", _CFG2_CASES, ids=[f"M{m}-K{k}-N{n}-cfg{c}" for m, k, n, c in _CFG2_CASES])
+def test_gemm_cfg2_grid_full_size_sampled_rows(M, K, N, cfg):
+    """BASELINE cfg2: M in {128, 1024, 4096, 8192} x (K, N) in {(2816, 2816), (2816, 8448), (4096, 14336)}, full-size
+    launch, bf16 out with the fused global-scale multiply, oracle on 66 rows (W4A4 bar)."""
+    p = require_gpu()
+    xq, xs, gx, wq, ws, gw, rows, ref = _cfg2_operands(p, M, K, N)
+    p.set_gemm_tile_config(cfg)
+    try:
+        Y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+        p.gemm(xq, xs, 1.0 / float(gx), wq, ws, 1.0 / float(gw), out=Y)
+        torch.cuda.synchronize()
+    finally:
+        p.set_gemm_tile_config(0)
+    assert p.read_device_error() == 0
+    assert not torch.isnan(Y).any()                      # every output written (full-size launch)
+    ok, msg = gate_w4a4(Y[torch.from_numpy(rows).cuda()].float().cpu().numpy(), ref)
+    assert ok, msg

@@ -8,7 +8,8 @@ Stage by stage:
   down      given the device's own intermediate, the combined output is within the W4A4 GEMM bar
             |Y - Yref| <= 1e-2 |Yref| + 1e-3 max|Yref|;
   end to end relative Frobenius error <= 2e-2 against the fully independent oracle.
-Routing for the expert stages is taken from the device (SURVEY hard part iv: near-tie routing flips)."""
+Routing for the expert stages is taken from the device: at a near-tie between the 8th and 9th expert the fp32
+logits of the device and the float64 oracle may pick different experts, which is not an expert-stage error."""
 import numpy as np
 import pytest
 import torch

@@ -47,3 +47,16 @@ def test_swizzle_matches_reference_binary():
                                outer, k)
         assert np.array_equal(out, orc.swizzle_scales(logical, outer, k))
         assert np.array_equal(out, native.swizzle(logical, outer, k))
+
+
+def test_c_dequantize_matches_numpy_oracle():
+    """The threaded C dequantiser (used by the large GPU parity tests) gives the numpy oracle's float64 values."""
+    import native
+    import nvfp4_oracle as orc
+    rng = np.random.default_rng(3)
+    for rows, k in [(1, 16), (37, 96), (300, 2816)]:
+        pk = rng.integers(0, 256, (rows, k // 2), dtype=np.uint8)
+        sf = rng.integers(0, 0x7F, (rows, k // 16), dtype=np.uint8)
+        sf[0, 0] = 0x80                                     # the oracle's zero-block byte
+        g = np.float32(2688.0 / 3.7)
+        assert np.array_equal(native.dequantize(pk, sf, g), orc.dequantize(pk, sf, g))
