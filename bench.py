@@ -458,7 +458,7 @@ class MoeWorkload:
         self.units_per_step = T
         self.kernel_flops = 2.0 * T * topk * (2 * I) * H          # grouped gate/up GEMM, routed rows only
         self.step_flops = 2.0 * T * topk * 3 * I * H + 2.0 * T * E * H
-        self.launches_per_step = 12   # amax, router GEMM + top-k, hist/plan/rank/pad/scatter, gate/up, down, combine
+        self.launches_per_step = 9    # amax, router GEMM + top-k, hist-rank/plan/quantise-scatter, gate/up, down, combine
         self.kernel_name = "nvf4_gemm_kernel<GroupedSched, GateUpEpi> (grouped gate/up, GELU + NVFP4 requant)"
         self.config = {"workload": "cfg3 MoE FFN layer", "tokens": T, "hidden": H, "experts": E, "inter": I,
                        "topk": topk, "router": "bf16 [128, 2816], softmax-top8-renorm",
@@ -613,15 +613,17 @@ class EpWorkload:
         torch.cuda.synchronize()
         del cal_ws
         self.units_per_step = T                                   # rows of this rank; value() scales by G
-        self.kernel_name = ("one MoE layer (dispatch with fused quantiser, grouped gate/up and down GEMMs, combine)"
+        self.kernel_name = ("one MoE layer with its router (nvfp4b_moe_layer: router GEMM, top-k + dispatch ranking, "
+                            "plan, quantise-scatter, grouped gate/up and down GEMMs, combine)"
                             if exchange == "local" else
                             "expert side of one layer (record scatter, grouped gate/up and down GEMMs, rows stored "
                             "back), including its wait for the other ranks' records")
         self.traffic_key = "ep" if exchange == "local" else None
-        # one amax, then per layer: router x2 + dispatch x4, expert x8, combine with the next input fused (p2p); the
-        # single-GPU layer's hist/plan/rank/pad/quant-scatter, gate/up, down, combine (local); + the amax of the
-        # next input (nccl, where the combine has no fused output)
-        self.launches_per_step = {"local": 10, "p2p": 15, "nccl": 16}[exchange] * L + 1
+        # one amax, then per layer -- local (nvfp4b_moe_layer): router GEMM, top-k + chunk ranking, plan,
+        # quantise-scatter, gate/up, down, combine; p2p: router x2, hist-rank, plan, pack, then meta, hist-rank, plan,
+        # scatter, gate/up, down, and the combine with the next input fused; nccl: the same plus the amax of the next
+        # input (its combine has no fused output)
+        self.launches_per_step = {"local": 7, "p2p": 12, "nccl": 13}[exchange] * L + 1
         self.kernel_flops = 2.0 * T * topk * 3 * I * H            # expert GEMMs of one layer at even routing
         self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
         self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_total": T * world,
@@ -640,10 +642,11 @@ class EpWorkload:
         self.res.copy_(self.x0)
         p.amax(self.x, out=self.amax)
         for li, Ld in enumerate(self.layers):
-            p.moe_route(self.x, Ld["proj"], k, Ld["ops"].src_ws, ids=Ld["ids"], weights=Ld["w"])
-            # residual stream: res += MoE(x); the combine also leaves x = bf16(res) and its amax for the next layer
-            Ld["layer"].forward(self.x, Ld["ids"], Ld["w"], self.res, in_amax=self.amax, accumulate=True,
-                                mark=mark if li == 0 else None, x_next=self.x, amax_next=self.amax)
+            # router + layer on the residual stream: res += MoE(x); the combine also leaves x = bf16(res) and its
+            # amax for the next layer (one GPU: the router fused into the layer, nvfp4b_moe_layer)
+            Ld["layer"].forward_routed(self.x, Ld["proj"], Ld["ids"], Ld["w"], self.res, in_amax=self.amax,
+                                       accumulate=True, mark=mark if li == 0 else None, x_next=self.x,
+                                       amax_next=self.amax)
 
     def value(self, seconds_per_step):
         return self.units_per_step / seconds_per_step
@@ -680,15 +683,15 @@ class EpWorkload:
 
     def layer_bytes(self):
         """Algorithmic DRAM bytes of the timed part of one layer: the NVFP4 weights (codes + tile scales) of every
-        local expert that received a row, read once, plus the layer's activations -- local layer: x in (bf16),
-        the residual read and written (fp32) and the next input out (bf16); expert side of a rank: the records in
-        (one per assignment) and one fp16 row per record out."""
+        local expert that received a row, read once, plus the layer's activations -- local layer (router included):
+        x in (bf16), the residual read and written (fp32), the next input out (bf16) and the bf16 router weights;
+        expert side of a rank: the records in (one per assignment) and one fp16 row per record out."""
         counts = self._rows_per_expert()
         hit = sum(1 for c in counts if c > 0)
         n = sum(counts)
         w = hit * self._expert_bytes()
         if self.exchange == "local":
-            act = self.T * self.H * (2 + 4 + 4 + 2)
+            act = self.T * self.H * (2 + 4 + 4 + 2) + self.E * self.H * 2     # + the bf16 router weights
         else:
             act = n * (self.pkg.ep_record_bytes(self.H) + 2 * self.H)
         return {"weights": w, "activations": act, "total": w + act, "experts_hit": hit, "rows": n}

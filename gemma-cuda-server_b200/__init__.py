@@ -9,7 +9,8 @@ Two layers:
   include/fp4_gemm.h:13-35 of the reference): ``nvfp4_quantize_activations``, ``nvfp4_scale_buffer_bytes``,
   ``nvfp4_swizzle_scales``, ``nvfp4_gemm``, ``w4a16_gemm``, ``fp4_gemv`` -- device pointers as torch tensors;
 * tensor-level helpers used by the tests and the benchmark: ``quantize``, ``amax``, ``gemm``, ``linear``, the MoE
-  layer (``moe_route``, ``moe_forward`` with its chained and fused-norm forms, ``MoeExperts``), and the
+  layer (``moe_route``, ``moe_forward`` with its chained and fused-norm forms, ``moe_layer`` with the router fused
+  in, ``MoeExperts``), and the
   expert-parallel entry points (``ep_*`` over NCCL slots, ``ep_p2p_*`` over peer memory with the ``ipc_*`` set-up
   helpers; ``expert_parallel.py`` orchestrates them).
 """
@@ -256,6 +257,8 @@ def _moe_sigs():
                                      ctypes.c_float, ctypes.c_float, _P, ctypes.c_int, _P, _P], ctypes.c_int),
         "nvfp4b_moe_forward_chain": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts),
                                       ctypes.c_float, _P, _P, ctypes.c_int, _P, _P, _P, _P], ctypes.c_int),
+        "nvfp4b_moe_layer": ([_P, ctypes.c_int, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.POINTER(_Experts),
+                              ctypes.c_float, _P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_calibrate": ([_P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.POINTER(_Experts), ctypes.c_float,
                                   _P, _P, _P, _P], ctypes.c_int),
         "nvfp4b_moe_workspace_view": ([_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -372,6 +375,27 @@ def moe_forward(x, ids, weights, experts: MoeExperts, workspace, in_gscale: floa
     _check("moe_forward", _moe_sigs().nvfp4b_moe_forward(
         _ptr(x), T, _ptr(ids), _ptr(weights), topk, ctypes.byref(st), float(in_gscale or 0.0), _ptr(in_amax),
         _ptr(out), flags, _ptr(workspace), _stream(stream)))
+    return out
+
+
+def moe_layer(x, proj, topk: int, experts: MoeExperts, workspace, ids=None, weights=None, per_expert_scale=None,
+              norm: bool = False, in_gscale: float | None = None, in_amax=None, out=None, accumulate: bool = False,
+              atomic: bool = False, x_next=None, amax_next=None, stream=None):
+    """Router + MoE layer in one call (nvfp4b_moe_layer): the same as moe_route followed by moe_forward (with
+    x_next / amax_next: the chained form).  Returns out; ids [T, topk] / weights [T, topk] receive the routing."""
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty((T, experts.H), dtype=torch.float32, device=x.device)
+    if ids is None:
+        ids = torch.empty((T, topk), dtype=torch.int32, device=x.device)
+    if weights is None:
+        weights = torch.empty((T, topk), dtype=torch.float32, device=x.device)
+    st = experts.struct()
+    flags = (MOE_ACCUMULATE if accumulate else 0) | (MOE_ATOMIC if atomic else 0)
+    _check("moe_layer", _moe_sigs().nvfp4b_moe_layer(
+        _ptr(x), T, _ptr(proj), topk, _ptr(per_expert_scale), 1 if norm else 0, ctypes.byref(st),
+        float(in_gscale or 0.0), _ptr(in_amax), _ptr(out), flags, _ptr(ids), _ptr(weights), _ptr(workspace),
+        _ptr(x_next), _ptr(amax_next), _stream(stream)))
     return out
 
 

@@ -65,6 +65,7 @@ struct Workspace {
     int* m_tiles;
     int* tile_expert;
     int* dest;
+    int* lrank;           // [T*topk] stable rank of each assignment among its chunk's assignments to the same expert
     int* row_token;
     float* row_weight;
     int* row_assign;
@@ -81,10 +82,25 @@ struct Workspace {
     size_t bytes;
 };
 
+// Chunks of the dispatch ranking: kChunk assignments (ids given), or the tokens of one block of the fused router
+// top-k, at least 8 (one per warp; router_topk_tpw).
+inline int max_chunks(int T, int topk) {
+    const int a = (T * topk + kChunk - 1) / kChunk, b = (T + 7) / 8;
+    return a > b ? a : b;
+}
+
+// Tokens per warp of the fused router top-k: one (the most parallel) unless that makes more than two blocks of 8
+// warps per SM; then 2, 4, ... while a block's chunk of 8 * tpw * topk assignments stays within 256.
+inline int router_topk_tpw(int T, int topk, int sms) {
+    int tpw = 1;
+    while (16 * tpw * topk <= 256 && (T + 8 * tpw - 1) / (8 * tpw) > 2 * sms) tpw *= 2;
+    return tpw;
+}
+
 Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     Workspace w{};
     const int n_assign = T * topk;
-    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
+    const int n_chunks = max_chunks(T, topk);
     const int rows = max_rows_for(T, E, topk);
     char* p = static_cast<char*>(base);
     size_t off = 0;
@@ -97,6 +113,7 @@ Workspace carve(void* base, int T, int H, int I, int E, int topk) {
     w.m_tiles = (int*)take(4);
     w.tile_expert = (int*)take((size_t)(rows / 128) * 4);
     w.dest = (int*)take((size_t)n_assign * 4);
+    w.lrank = (int*)take((size_t)n_assign * 4);
     w.row_token = (int*)take((size_t)rows * 4);
     w.row_weight = (float*)take((size_t)rows * 4);
     w.row_assign = (int*)take((size_t)rows * 4);
@@ -144,32 +161,27 @@ struct RouterEpi {
 
 using RouterCfg = KCfg<128, 6, 2, 4, Kind::BF16>;
 
+// Top-k of token t, one warp: sum of the split-K partial logits in split order (every split's loads issued before
+// the first add), optional per-token norm factor, softmax over E experts, top-k with ties to the lower id,
+// renormalised and times per_expert_scale.  Lane j < topk returns the j-th choice in *id / *wt (other lanes: -1).
 template <int EPL>
-__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits,
-                                                          long long split_stride, int T, int E, int topk,
-                                                          const uint16_t* __restrict__ xnorm, int H,
-                                                          const float* __restrict__ pes, int* __restrict__ ids,
-                                                          float* __restrict__ wout) {
-    const int lane = threadIdx.x & 31;
-    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (t >= T) return;
-    // Sum of the split-K partial logits in split order; four splits' loads are issued together.
+__device__ __forceinline__ void route_token(const float* __restrict__ partial, int splits, long long split_stride,
+                                            int t, int E, int topk, const uint16_t* __restrict__ xnorm, int H,
+                                            const float* __restrict__ pes, int lane, int* id, float* wt) {
     float l[EPL];
 #pragma unroll
     for (int i = 0; i < EPL; ++i) l[i] = 0.f;
     const float* pt = partial + (long long)t * E + lane;
-    for (int s0 = 0; s0 < splits; s0 += 4) {
-        float v[4][EPL];
+    float v[kRouterMaxSplits][EPL];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < kRouterMaxSplits; ++u)
 #pragma unroll
-            for (int i = 0; i < EPL; ++i) v[u][i] = s0 + u < splits ? __ldg(pt + (s0 + u) * split_stride + 32 * i) : 0.f;
+        for (int i = 0; i < EPL; ++i) v[u][i] = u < splits ? __ldg(pt + u * split_stride + 32 * i) : 0.f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < kRouterMaxSplits; ++u)
 #pragma unroll
-            for (int i = 0; i < EPL; ++i)
-                if (s0 + u < splits) l[i] += v[u][i];
-    }
+        for (int i = 0; i < EPL; ++i)
+            if (u < splits) l[i] += v[u][i];
     if (xnorm) {   // reference k_router_hn: x * rsqrt(mean(x^2) + 1e-6) * H^-0.5 (scale folded into proj)
         const uint16_t* xr = xnorm + (long long)t * H;
         float ss = 0.f;
@@ -202,7 +214,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 #pragma unroll
     for (int i = 0; i < EPL; ++i) p[i] = p[i] / sum;
     unsigned used = 0u;
-    int my_id = 0;
+    int my_id = -1;
     float my_p = 0.f, wsum = 0.f;
     for (int j = 0; j < topk; ++j) {
         float bv = -1.f;
@@ -220,10 +232,29 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
         if (lane == j) { my_id = be; my_p = bv; }
         wsum += bv;
     }
+    float w = 0.f;
     if (lane < topk) {
-        float w = my_p / wsum;
+        w = my_p / wsum;
         if (pes) w *= __ldg(pes + my_id);
-        ids[(long long)t * topk + lane] = my_id;
+    }
+    *id = my_id;
+    *wt = w;
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ partial, int splits,
+                                                          long long split_stride, int T, int E, int topk,
+                                                          const uint16_t* __restrict__ xnorm, int H,
+                                                          const float* __restrict__ pes, int* __restrict__ ids,
+                                                          float* __restrict__ wout) {
+    const int lane = threadIdx.x & 31;
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (t >= T) return;
+    int id;
+    float w;
+    route_token<EPL>(partial, splits, split_stride, t, E, topk, xnorm, H, pes, lane, &id, &w);
+    if (lane < topk) {
+        ids[(long long)t * topk + lane] = id;
         wout[(long long)t * topk + lane] = w;
     }
 }
@@ -232,127 +263,145 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // 2. dispatch
 // ---------------------------------------------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(256) moe_hist_kernel(const int* __restrict__ ids, int n_assign, int E,
-                                                       int* __restrict__ hist) {
-    __shared__ int h[256];
-    for (int i = threadIdx.x; i < E; i += blockDim.x) h[i] = 0;
+// Called by all 256 threads of a block that owns one chunk of at most 256 assignments (thread i: assignment i of the
+// chunk, expert e, or -1 for none): writes the chunk's histogram hist[chunk][e] and the stable rank of every
+// assignment among the chunk's earlier assignments to the same expert (lrank; warps in order, lanes in order), so
+// that the final row of assignment a is chunk_base[chunk][e] + lrank[a] once the plan kernel has laid out the
+// segments.  Assignments with an id outside [0, E) get lrank -1 (they are dropped).
+__device__ __forceinline__ void chunk_hist_rank(int e, long long a, bool valid, int E, int chunk,
+                                                int* __restrict__ hist, int* __restrict__ lrank) {
+    __shared__ int wcnt[8][256];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < 8 * 256; i += 256) (&wcnt[0][0])[i] = 0;
+    if (!(e >= 0 && e < E)) e = -1;
     __syncthreads();
-    const int base = blockIdx.x * kChunk;
-    const int end = min(base + kChunk, n_assign);
-    for (int a = base + threadIdx.x; a < end; a += blockDim.x) {
-        const int e = __ldg(ids + a);
-        if (e >= 0 && e < E) atomicAdd(&h[e], 1);
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+        int r = -1;
+        if (e >= 0) {
+            r = rank;
+            for (int q = 0; q < warp; ++q) r += wcnt[q][e];
+        }
+        lrank[a] = r;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < E; i += blockDim.x) hist[blockIdx.x * E + i] = h[i];
+    for (int i = tid; i < E; i += 256) {
+        int c = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) c += wcnt[q][i];
+        hist[(long long)chunk * E + i] = c;
+    }
 }
 
-__global__ void __launch_bounds__(256) moe_plan_kernel(const int* __restrict__ hist, int n_chunks, int E,
-                                                       int* __restrict__ chunk_base, int* __restrict__ seg_start,
-                                                       int* __restrict__ seg_count, int* __restrict__ m_tiles,
-                                                       int* __restrict__ tile_expert) {
-    __shared__ int padded[257];
-    const int e = threadIdx.x;
-    int total = 0;
-    if (e < E)
-        for (int c = 0; c < n_chunks; ++c) total += hist[c * E + e];
-    // inclusive scan of the padded segment sizes (warp scans, then the 8 warp totals) -> padded[e + 1] = end of e
-    __shared__ int wsum[8];
-    const int lane = e & 31, wid = e >> 5;
-    int v = (e < E) ? (total + 127) / 128 * 128 : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
-        if (lane >= o) v += u;
+// ids given: one chunk of kChunk assignments per block.
+__global__ void __launch_bounds__(256) moe_hist_rank_kernel(const int* __restrict__ ids, int n_assign, int E,
+                                                            int* __restrict__ hist, int* __restrict__ lrank) {
+    static_assert(kChunk == 256, "one assignment per thread");
+    const long long a = (long long)blockIdx.x * kChunk + threadIdx.x;
+    const bool valid = a < n_assign;
+    chunk_hist_rank(valid ? __ldg(ids + a) : -1, a, valid, E, blockIdx.x, hist, lrank);
+}
+
+// The router's top-k fused with the dispatch ranking: a block routes tpb = 8 * tpw consecutive tokens (warp w takes
+// tokens w, w + 8, ...), so its tpb * topk (<= 256) assignments are one chunk, which it then ranks and counts as
+// moe_hist_rank_kernel does (chunk size tpb * topk instead of kChunk).
+template <int EPL>
+__global__ void __launch_bounds__(256) router_topk_rank_kernel(const float* __restrict__ partial, int splits,
+                                                               long long split_stride, int T, int E, int topk,
+                                                               const uint16_t* __restrict__ xnorm, int H,
+                                                               const float* __restrict__ pes, int* __restrict__ ids,
+                                                               float* __restrict__ wout, int* __restrict__ hist,
+                                                               int* __restrict__ lrank, int tpw) {
+    __shared__ int s_ids[256];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tpb = 8 * tpw;
+    const int t0 = blockIdx.x * tpb;
+    for (int lt = warp; lt < tpb; lt += 8) {
+        const int t = t0 + lt;
+        int id = -1;
+        float w = 0.f;
+        if (t < T) route_token<EPL>(partial, splits, split_stride, t, E, topk, xnorm, H, pes, lane, &id, &w);
+        if (lane < topk) {
+            s_ids[lt * topk + lane] = id;
+            if (t < T) {
+                ids[(long long)t * topk + lane] = id;
+                wout[(long long)t * topk + lane] = w;
+            }
+        }
     }
-    if (lane == 31) wsum[wid] = v;
     __syncthreads();
-    int off = 0;
-    for (int q = 0; q < wid; ++q) off += wsum[q];
-    padded[e + 1] = v + off;
-    if (e == 0) padded[0] = 0;
+    const int n = min(tpb, T - t0) * topk;
+    const bool valid = (int)threadIdx.x < n;
+    chunk_hist_rank(valid ? s_ids[threadIdx.x] : -1, (long long)t0 * topk + threadIdx.x, valid, E, blockIdx.x,
+                    hist, lrank);
+}
+
+// Segment layout from the chunk histograms, one block of kPlanThreads: 4 threads per expert (E <= 256), thread q of
+// expert e owning the q-th quarter of the chunks, so the histogram column is read with 4-way parallelism and a few
+// loads in flight per thread.  seg_count[e] = total rows of e; seg_start[e] = start of its segment (segments padded
+// to 128 rows, in expert order); chunk_base[c][e] = seg_start[e] + rows of e in chunks before c; tile_expert[] and
+// *m_tiles describe the 128-row blocks for the grouped GEMM scheduler.
+constexpr int kPlanThreads = 1024;
+__global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(const int* __restrict__ hist, int n_chunks, int E,
+                                                                int* __restrict__ chunk_base,
+                                                                int* __restrict__ seg_start,
+                                                                int* __restrict__ seg_count, int* __restrict__ m_tiles,
+                                                                int* __restrict__ tile_expert) {
+    __shared__ int part[4][256];
+    __shared__ int padded[257];
+    __shared__ int wsum[8];
+    const int e = threadIdx.x & 255, q = threadIdx.x >> 8;
+    const int per = (n_chunks + 3) / 4;
+    const int c0 = q * per, c1 = min(n_chunks, c0 + per);
+    int sum = 0;
+    if (e < E) {
+        int c = c0;
+        for (; c + 4 <= c1; c += 4) {
+            const int h0 = __ldg(hist + (long long)c * E + e), h1 = __ldg(hist + (long long)(c + 1) * E + e);
+            const int h2 = __ldg(hist + (long long)(c + 2) * E + e), h3 = __ldg(hist + (long long)(c + 3) * E + e);
+            sum += (h0 + h1) + (h2 + h3);
+        }
+        for (; c < c1; ++c) sum += __ldg(hist + (long long)c * E + e);
+    }
+    part[q][e] = sum;
+    __syncthreads();
+    const int total = part[0][e] + part[1][e] + part[2][e] + part[3][e];
+    if (q == 0) {   // inclusive scan of the padded segment sizes -> padded[e + 1] = end of segment e
+        const int lane = e & 31, wid = e >> 5;
+        int v = (e < E) ? (total + 127) / 128 * 128 : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
+            if (lane >= o) v += u;
+        }
+        if (lane == 31) wsum[wid] = v;
+        padded[e + 1] = v;      // within the warp; the earlier warps' totals are added below
+        if (e == 0) padded[0] = 0;
+    }
+    __syncthreads();
+    if (q == 0) {
+        int off = 0;
+        for (int w = 0; w < (e >> 5); ++w) off += wsum[w];
+        padded[e + 1] += off;
+    }
     __syncthreads();
     if (e < E) {
         const int start = padded[e];
-        seg_start[e] = start;
-        seg_count[e] = total;
+        if (q == 0) {
+            seg_start[e] = start;
+            seg_count[e] = total;
+        }
         int run = start;
-        for (int c = 0; c < n_chunks; ++c) {
-            chunk_base[c * E + e] = run;
-            run += hist[c * E + e];
+        for (int qq = 0; qq < q; ++qq) run += part[qq][e];
+        for (int c = c0; c < c1; ++c) {
+            chunk_base[(long long)c * E + e] = run;
+            run += __ldg(hist + (long long)c * E + e);
         }
-        for (int r = start; r < padded[e + 1]; r += 128) tile_expert[r / 128] = e;
+        for (int r = start + 128 * q; r < padded[e + 1]; r += 512) tile_expert[r / 128] = e;
     }
-    if (e == 0) *m_tiles = padded[E] / 128;
-}
-
-// Stable rank of every assignment inside its expert segment: assignments are visited in index order (rounds of
-// 256, warps in order, lanes in order) so rows keep (token, slot) order.
-__global__ void __launch_bounds__(256) moe_rank_kernel(const int* __restrict__ ids, const float* __restrict__ w,
-                                                       int n_assign, int E, int topk,
-                                                       const int* __restrict__ chunk_base, int* __restrict__ dest,
-                                                       int* __restrict__ row_token, float* __restrict__ row_weight,
-                                                       int* __restrict__ row_assign) {
-    __shared__ int run[256];
-    __shared__ int wcnt[8][256];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < E; i += 256) run[i] = chunk_base[blockIdx.x * E + i];
-    for (int i = tid; i < 8 * 256; i += 256) (&wcnt[0][0])[i] = 0;
-    __syncthreads();
-    const int base = blockIdx.x * kChunk;
-    for (int round = 0; round < kChunk / 256; ++round) {
-        const int a = base + round * 256 + tid;
-        int e = -1;
-        if (a < n_assign) {
-            e = __ldg(ids + a);
-            if (e < 0 || e >= E) e = -1;
-        }
-        const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
-        const int rank = __popc(peers & ((1u << lane) - 1u));
-        if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
-        __syncthreads();
-        if (e >= 0) {
-            int row = run[e] + rank;
-            for (int q = 0; q < warp; ++q) row += wcnt[q][e];
-            dest[a] = row;
-            row_token[row] = a / topk;
-            row_weight[row] = __ldg(w + a);
-            row_assign[row] = a;
-        } else if (a < n_assign) {
-            dest[a] = -1;
-        }
-        __syncthreads();
-        for (int i = tid; i < E; i += 256) {
-            int s = 0;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) { s += wcnt[q][i]; wcnt[q][i] = 0; }
-            run[i] += s;
-        }
-        __syncthreads();
-    }
-}
-
-// Padding rows of every segment: no token, zero weight, zero scales (so their products are exactly zero).
-__global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ seg_start,
-                                                      const int* __restrict__ seg_count, int kb, int tile_cols,
-                                                      uint8_t* __restrict__ a_scales, int* __restrict__ row_token,
-                                                      float* __restrict__ row_weight, int* __restrict__ row_assign,
-                                                      float* __restrict__ row_gscale) {
-    const int e = blockIdx.x;
-    const int start = seg_start[e], count = seg_count[e];
-    const int pad0 = start + count, pad1 = start + (count + 127) / 128 * 128;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = pad0 + warp; r < pad1; r += 8) {      // warp per padding row, lanes along its 4-block scale words
-        uint8_t* row_sf = a_scales + (long long)(r >> 7) * tile_cols * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4;
-        for (int tc = lane; tc < tile_cols; tc += 32) *reinterpret_cast<uint32_t*>(row_sf + (long long)tc * 512) = 0u;
-        if (lane == 0) {
-            row_token[r] = -1;
-            row_weight[r] = 0.f;
-            row_assign[r] = -1;
-            if (row_gscale) row_gscale[r] = 1.f;     // any finite scale: padding rows hold zero codes
-        }
-    }
-    (void)kb;
+    if (threadIdx.x == 0) *m_tiles = padded[E] / 128;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -362,12 +411,22 @@ __global__ void __launch_bounds__(256) moe_pad_kernel(const int* __restrict__ se
 constexpr int kScatterWarps = 6;   // warps per token in the quantise-and-scatter kernel (6 x 32 lanes >= H/16 = 176)
 
 // kScatterWarps warps per token: warp `part` quantises every kScatterWarps-th run of 32 blocks of x[t] once and
-// writes each block to all of the token's destination rows.  With norm_w (bf16 [H]) the row is RMS-normalised first,
-// x * rsqrt(mean(x^2) + eps) * norm_w in fp32 (the reference's rmsnorm, kernels/elementwise.cu:10-22, applied to
-// the MoE input as pre_feedforward_layernorm_2 in src/forward.cu:535), and the fp32 values are quantised: the
-// normalised activations are never stored.
+// writes each block to all of the token's destination rows.  The destination row of assignment a = t * topk + j is
+// chunk_base[a / chunk][e] + lrank[a] (e = ids[a]; the plan kernel laid out the segments, the ranking kernel ranked
+// the chunk of `chunk` assignments); warp 0 of the token also records the row's metadata (dest, token, weight,
+// assignment).  Rows of segment padding are not written at all: the GEMM epilogues tell them apart by the segment
+// bounds, and a padding row's products (whatever its stale codes and scales) land only in that row's outputs, which
+// are never stored.  With norm_w (bf16 [H]) the row is RMS-normalised first, x * rsqrt(mean(x^2) + eps) * norm_w in
+// fp32 (the reference's rmsnorm, kernels/elementwise.cu:10-22, applied to the MoE input as pre_feedforward_layernorm_2
+// in src/forward.cu:535), and the fp32 values are quantised: the normalised activations are never stored.
 __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* __restrict__ x, int T, int H,
-                                                                int topk, const int* __restrict__ dest,
+                                                                int topk, const int* __restrict__ ids,
+                                                                const float* __restrict__ weights, int E,
+                                                                const int* __restrict__ chunk_base,
+                                                                const int* __restrict__ lrank, int chunk,
+                                                                int* __restrict__ dest, int* __restrict__ row_token,
+                                                                float* __restrict__ row_weight,
+                                                                int* __restrict__ row_assign,
                                                                 float gscale, const float* __restrict__ d_amax,
                                                                 uint8_t* __restrict__ a_codes,
                                                                 uint8_t* __restrict__ a_scales, int tile_cols,
@@ -377,7 +436,21 @@ __global__ void __launch_bounds__(256) moe_quant_scatter_kernel(const uint16_t* 
     const int t = gw / kScatterWarps, part = gw % kScatterWarps;
     if (t >= T) return;
     const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
-    const int my_dest = lane < topk ? __ldg(dest + (long long)t * topk + lane) : -1;
+    int my_dest = -1;
+    if (lane < topk) {
+        const int a = t * topk + lane;
+        const int e = __ldg(ids + a);
+        const int r = __ldg(lrank + a);
+        if (e >= 0 && e < E && r >= 0) my_dest = __ldg(chunk_base + (a / chunk) * E + e) + r;
+        if (part == 0) {
+            dest[a] = my_dest;
+            if (my_dest >= 0) {
+                row_token[my_dest] = t;
+                row_weight[my_dest] = __ldg(weights + a);
+                row_assign[my_dest] = a;
+            }
+        }
+    }
     const int kb = H >> 4;
     const uint16_t* xr = x + (long long)t * H;
     float inv = 1.f;
@@ -523,12 +596,13 @@ struct GateUpEpi {
     const float* d_in_amax;
     const float* row_gscale;   // if set: per-row activation global scale (overrides in_gscale / d_in_amax)
     float* h_amax;   // calibration output
-    const int* row_token;
+    const int* seg_start;      // [E] first row of each expert segment
+    const int* seg_count;      // [E] real rows of each expert segment (the rest up to 128 is padding)
 
     __device__ __forceinline__ void finish() const {}
     // Rows of expert-segment padding hold no token: a warp whose 32 rows are all padding skips its work.
     __device__ __forceinline__ bool row_live(const TileInfo& ti, int row) const {
-        return __ldg(row_token + (long long)ti.a_row + row) >= 0;
+        return ti.a_row + row - __ldg(seg_start + ti.expert) < __ldg(seg_count + ti.expert);
     }
 
     template <int CH>
@@ -542,7 +616,7 @@ struct GateUpEpi {
         const int jb0 = (ti.n0 + col_base) >> 5;          // first 16-wide block of h handled by this thread
         if constexpr (CALIBRATE) {
             float amax = 0.f;
-            const bool real = __ldg(row_token + m) >= 0;    // padding rows hold no token (-1)
+            const bool real = row_live(ti, row);            // padding rows hold no token
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
                 if ((jb0 + c) * 16 >= I || !real) continue;
@@ -616,6 +690,8 @@ struct DownEpi {
     const float* weights;
     const float* w2_gscale;
     const float* a2_gscale;
+    const int* seg_start;      // [E] first row of each expert segment
+    const int* seg_count;      // [E] real rows of each expert segment (the rest up to 128 is padding)
     // Expert parallelism over peer memory (DETERMINISTIC only): the row of received slot a = s * capacity + j goes
     // to source rank s's return rows, row rank * capacity + j, instead of y[a]; the last epilogue warp of the grid
     // then raises the rows-landed flags (flags[s][G + rank]).
@@ -624,15 +700,17 @@ struct DownEpi {
     unsigned* state = nullptr;
     int rank = 0, G = 0, capacity = 0;
     bool transpose = false;     // rows through the shared-memory transpose (launched with DownTransposeCfg)
+    float* zero_word = nullptr; // if set, stored as 0 once by the kernel (the chained amax the combine accumulates)
 
-    // Padding rows of an expert segment (row_assign -1) produce nothing: a warp whose 32 rows are all padding skips
-    // its work.
+    // Padding rows of an expert segment produce nothing (their row_assign is never written): a warp whose 32 rows
+    // are all padding skips its work.
     __device__ __forceinline__ bool row_live(const TileInfo& ti, int row) const {
-        return __ldg(row_assign + (long long)ti.a_row + row) >= 0;
+        return ti.a_row + row - __ldg(seg_start + ti.expert) < __ldg(seg_count + ti.expert);
     }
 
     // Every epilogue warp (warps 4.. of every CTA) calls this once after its last tile.
     __device__ __forceinline__ void finish() const {
+        if (zero_word && blockIdx.x == 0 && threadIdx.x == 128) *zero_word = 0.0f;
         if constexpr (DETERMINISTIC) {
             if (!peer_back) return;
             __syncwarp();
@@ -661,7 +739,7 @@ struct DownEpi {
     __device__ __forceinline__ void process(const TileInfo& ti, int row, int col_base, const uint32_t (&r)[CH][32],
                                             uint8_t* esm) const {
         const long long m = (long long)ti.a_row + row;
-        const int a = __ldg(row_assign + m);
+        const int a = row_live(ti, row) ? __ldg(row_assign + m) : -1;
         const int e = ti.expert;
         const float s = a >= 0 ? __ldg(weights + a) * __frcp_rn(__ldg(a2_gscale + e) * __ldg(w2_gscale + e)) : 0.f;
         if constexpr (DETERMINISTIC) {
@@ -844,14 +922,17 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hi
 
 // Warp per token: quantise x[t] once (dynamic or static global scale), write one record per routed slot.
 // kPackWarps warps per token, each quantising every kPackWarps-th run of 32 blocks of x[t] and writing them to all
-// of the token's records.  slot[a] = d * capacity + (dest[a] - dst_start[d]) for the assignment's destination d
-// (dest = compact expert-sorted position), or -1 past the capacity (overflowed, not sent).  The record goes to
+// of the token's records.  slot[a] = d * capacity + (pos - dst_start[d]) for the assignment's destination d, where
+// pos = chunk_base[a / kChunk][e] + lrank[a] is its compact expert-sorted position, or -1 past the capacity
+// (overflowed, not sent).  The record goes to
 // records[slot], or with peers.recv to peer d's receive slot rank * capacity + (slot - d * capacity); the last
 // block then stores the per-destination counts, raises the records-landed flags and advances the layer epoch.
 constexpr int kPackWarps = 6;
 
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
-                                                      const int* __restrict__ dest, const int* __restrict__ ids,
+                                                      const int* __restrict__ chunk_base,
+                                                      const int* __restrict__ lrank, int E,
+                                                      const int* __restrict__ ids,
                                                       const float* __restrict__ weights, int experts_per_rank,
                                                       int capacity, const int* __restrict__ dst_start,
                                                       float gscale, const float* __restrict__ d_amax,
@@ -866,7 +947,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
         uint8_t* my_rec = nullptr;
         if (lane < topk) {
             const long long a = (long long)t * topk + lane;
-            const int pos = __ldg(dest + a);
+            const int e = __ldg(ids + a), r = __ldg(lrank + a);
+            const int pos = (e >= 0 && e < E && r >= 0) ? __ldg(chunk_base + (a / kChunk) * E + e) + r : -1;
             int my_slot = -1;
             if (pos >= 0) {
                 const int d = __ldg(ids + a) / experts_per_rank;
@@ -940,15 +1022,22 @@ __global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* records, in
     w[i] = meta.weight;
 }
 
-// Warp per received record: codes to its row of the padded expert-sorted operand, scales to the tile layout.
+// Warp per received record slot i: its row r = chunk_base[i / kChunk][e] + lrank[i] of the padded expert-sorted
+// operand (e = its local expert, -1 for an empty slot), codes to that row, scales to the tile layout, and the row's
+// metadata (slot, weight, the activation global scale the codes were made with).
 __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restrict__ records, int n, int H,
-                                                         const int* __restrict__ dest, uint8_t* __restrict__ a_codes,
-                                                         uint8_t* __restrict__ a_scales, float* __restrict__ row_gscale,
-                                                         int tile_cols) {
+                                                         const int* __restrict__ ep_ids, const float* __restrict__ ep_w,
+                                                         int E, const int* __restrict__ chunk_base,
+                                                         const int* __restrict__ lrank, int* __restrict__ dest,
+                                                         int* __restrict__ row_assign, float* __restrict__ row_weight,
+                                                         uint8_t* __restrict__ a_codes, uint8_t* __restrict__ a_scales,
+                                                         float* __restrict__ row_gscale, int tile_cols) {
     const int lane = threadIdx.x & 31;
     const int i = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
     if (i >= n) return;
-    const int r = __ldg(dest + i);
+    const int e = __ldg(ep_ids + i), rk = __ldg(lrank + i);
+    const int r = (e >= 0 && e < E && rk >= 0) ? __ldg(chunk_base + (i / kChunk) * E + e) + rk : -1;
+    if (lane == 0) dest[i] = r;
     if (r < 0) return;
     const uint8_t* rec = records + (size_t)i * ep_record_bytes(H);
     const int kb = H >> 4;
@@ -958,7 +1047,11 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint8_t* __restri
         a_scales[((long long)(r >> 7) * tile_cols + (b >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (b & 3)] =
             rec[(H / 2) + b];
     }
-    if (lane == 0) row_gscale[r] = reinterpret_cast<const EpMeta*>(rec + (H / 2) + (H / 16))->gscale;
+    if (lane == 0) {
+        row_gscale[r] = reinterpret_cast<const EpMeta*>(rec + (H / 2) + (H / 16))->gscale;
+        row_assign[r] = i;
+        row_weight[r] = __ldg(ep_w + i);
+    }
 }
 
 // out[t] (+)= sum_j y_back[slot[t*k + j]] in slot order (fp32 accumulation of the fp16 rows sent back).  One
@@ -1018,23 +1111,28 @@ int check_experts(const nvfp4b_moe_experts* ex) {
     return NVFP4B_OK;
 }
 
+// Dispatch: hist-rank (per chunk of kChunk assignments) -> plan (segment layout, one block) -> quantise-scatter
+// (rows from the plan and the chunk ranks, codes and scales of every real row, row metadata).  With ranked = true
+// the chunk histograms and ranks are already in the workspace (the fused router top-k wrote them for chunks of
+// `chunk` assignments) and the hist-rank launch is skipped.
 int dispatch(const void* x, int T, const int* ids, const float* weights, int topk, int H, int E, float in_gscale,
              const float* d_in_amax, const Workspace& w, cudaStream_t s, const uint16_t* norm_w = nullptr,
-             float eps = 0.f) {
+             float eps = 0.f, bool ranked = false, int chunk = kChunk) {
     const int n_assign = T * topk;
-    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
-    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
-    moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
-                                      w.tile_expert);
-    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
-                                             w.row_weight, w.row_assign);
+    const int n_chunks = (n_assign + chunk - 1) / chunk;
+    int st;
+    if (!ranked) {
+        st = launch_k(moe_hist_rank_kernel, dim3(n_chunks), dim3(256), 0, s, ids, n_assign, E, w.hist, w.lrank);
+        if (st) return st;
+    }
+    st = launch_k(moe_plan_kernel, dim3(1), dim3(kPlanThreads), 0, s, w.hist, n_chunks, E, w.chunk_base,
+                  w.seg_start, w.seg_count, w.m_tiles, w.tile_expert);
+    if (st) return st;
     const int tile_cols = (H / 16 + 3) / 4;
-    moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
-                                     w.row_weight, w.row_assign, nullptr);
-    moe_quant_scatter_kernel<<<(T * kScatterWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
-                                                         in_gscale, d_in_amax, w.a_codes, w.a_scales, tile_cols,
-                                                         norm_w, eps);
-    return launch_status();
+    return launch_k(moe_quant_scatter_kernel, dim3((T * kScatterWarps + 7) / 8), dim3(256), 0, s,
+                    static_cast<const uint16_t*>(x), T, H, topk, ids, weights, E, w.chunk_base, w.lrank, chunk,
+                    w.dest, w.row_token, w.row_weight, w.row_assign, in_gscale, d_in_amax, w.a_codes, w.a_scales,
+                    tile_cols, norm_w, eps);
 }
 
 template <bool CALIBRATE>
@@ -1074,7 +1172,8 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
     e.d_in_amax = d_in_amax;
     e.row_gscale = per_row_gscale ? w.row_gscale : nullptr;
     e.h_amax = h_amax;
-    e.row_token = w.row_token;
+    e.seg_start = w.seg_start;
+    e.seg_count = w.seg_count;
     return launch_core<GroupCfg>(ma, mb, cp, sc, e, sm_count(), s);
 }
 
@@ -1106,7 +1205,8 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
     sc.b_row_tiles_per_expert = (H + 127) / 128;
     sc.k_tiles = cp.k_tiles;
     if (deterministic) {
-        DownEpi<true> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
+        DownEpi<true> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale, w.seg_start,
+                        w.seg_count};
         if (peers) {
             e.peer_back = peers->back;
             e.peer_flags = peers->flags;
@@ -1116,14 +1216,13 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
             e.capacity = peers->capacity;
         }
         e.transpose = peers != nullptr || (long long)T * topk >= kDownTransposeRows;
+        // the chained amax is zeroed by the down kernel: every reader of the layer's input scale (the dispatch and
+        // the gate/up epilogue) has finished by then, and the combine that accumulates it runs after
+        e.zero_word = (out && next.x) ? next.amax : nullptr;
         static_assert(DownTransposeCfg::BM == DownCfg::BM && DownTransposeCfg::BN == DownCfg::BN, "same tiles, maps");
         st = e.transpose ? launch_core<DownTransposeCfg>(ma, mb, cp, sc, e, sm_count(), s)
                          : launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
         if (st || !out) return st;                  // out == nullptr: leave the weighted rows in w.y
-        if (next.x) {
-            const cudaError_t err = cudaMemsetAsync(next.amax, 0, sizeof(float), s);
-            if (err != cudaSuccess) return record_cuda_error(err);
-        }
         moe_combine_kernel<<<(unsigned)(((long long)T * (H / 8) + 255) / 256), 256, 0, s>>>(w.y, T, H, topk, out,
                                                                                       accumulate ? 1 : 0, next);
         return launch_status();
@@ -1132,7 +1231,8 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
         cudaError_t err = cudaMemsetAsync(out, 0, (size_t)T * H * sizeof(float), s);
         if (err != cudaSuccess) return record_cuda_error(err);
     }
-    DownEpi<false> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale};
+    DownEpi<false> e{w.y, out, H, topk, w.row_assign, weights, ex->w2_gscale, ex->a2_gscale, w.seg_start,
+                     w.seg_count};
     return launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
 }
 
@@ -1143,14 +1243,13 @@ int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weight
                 int* send_counts, int* overflow, cudaStream_t s) {
     const int n_assign = T * topk;
     const int n_chunks = (n_assign + kChunk - 1) / kChunk;
-    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
+    moe_hist_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist, w.lrank);
     ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, capacity, w.chunk_base, w.seg_count,
                                      w.seg_start, send_counts, overflow);
-    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
-                                             w.row_weight, w.row_assign);
-    ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
-                                                            ids, weights, E / G, capacity, w.seg_start, in_gscale,
-                                                            d_in_amax, records, w.ep_ids, EpPackPeers{});
+    ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk,
+                                                            w.chunk_base, w.lrank, E, ids, weights, E / G, capacity,
+                                                            w.seg_start, in_gscale, d_in_amax, records, w.ep_ids,
+                                                            EpPackPeers{});
     return launch_status();
 }
 
@@ -1162,11 +1261,9 @@ int ep_dispatch_p2p(const void* x, int T, int H, const int* ids, const float* we
     const int G = pr.G, capacity = pr.capacity;
     const int n_assign = T * topk;
     const int n_chunks = (n_assign + kChunk - 1) / kChunk;
-    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist);
+    moe_hist_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist, w.lrank);
     ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, capacity, w.chunk_base, w.seg_count,
                                      w.seg_start, w.ep_send, overflow);
-    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, weights, n_assign, E, topk, w.chunk_base, w.dest, w.row_token,
-                                             w.row_weight, w.row_assign);
     EpPackPeers pp;
     pp.recv = pr.recv;
     pp.counts = pr.counts;
@@ -1175,9 +1272,9 @@ int ep_dispatch_p2p(const void* x, int T, int H, const int* ids, const float* we
     pp.send_counts = w.ep_send;
     pp.rank = pr.rank;
     pp.G = G;
-    ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk, w.dest,
-                                                            ids, weights, E / G, capacity, w.seg_start, in_gscale,
-                                                            d_in_amax, nullptr, w.ep_ids, pp);
+    ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk,
+                                                            w.chunk_base, w.lrank, E, ids, weights, E / G, capacity,
+                                                            w.seg_start, in_gscale, d_in_amax, nullptr, w.ep_ids, pp);
     return launch_status();
 }
 
@@ -1194,15 +1291,12 @@ int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_count
                                                    peers ? peers->my_flags : nullptr, G,
                                                    peers ? peers->state : nullptr, err,
                                                    g_peer_wait_ns.load(std::memory_order_relaxed));
-    moe_hist_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist);
-    moe_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count, w.m_tiles,
-                                      w.tile_expert);
-    moe_rank_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, w.ep_w, n, E, 1, w.chunk_base, w.dest, w.row_token,
-                                             w.row_weight, w.row_assign);
+    moe_hist_rank_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist, w.lrank);
+    moe_plan_kernel<<<1, kPlanThreads, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count,
+                                               w.m_tiles, w.tile_expert);
     const int tile_cols = (H / 16 + 3) / 4;
-    moe_pad_kernel<<<E, 256, 0, s>>>(w.seg_start, w.seg_count, H / 16, tile_cols, w.a_scales, w.row_token,
-                                     w.row_weight, w.row_assign, w.row_gscale);
-    ep_scatter_kernel<<<(n + 7) / 8, 256, 0, s>>>(records, n, H, w.dest, w.a_codes, w.a_scales, w.row_gscale,
+    ep_scatter_kernel<<<(n + 7) / 8, 256, 0, s>>>(records, n, H, w.ep_ids, w.ep_w, E, w.chunk_base, w.lrank, w.dest,
+                                                  w.row_assign, w.row_weight, w.a_codes, w.a_scales, w.row_gscale,
                                                   tile_cols);
     int st = launch_status();
     if (st) return st;
@@ -1273,9 +1367,11 @@ extern "C" int nvfp4b_moe_workspace_view(void* workspace, int T, int H, int I, i
 
 // Router launch sequence (split-K bf16 GEMM into `partial`, then softmax/top-k); arguments already checked.
 // `partial` holds splits * T * E fp32 values, every one stored before it is read: nothing needs to start at zero.
+// With hist/lrank (the fused MoE layer) the top-k kernel also ranks each block's chunk of 8 * tpw tokens'
+// assignments for the dispatch (router_topk_rank_kernel).
 static int route_launch(const void* x, int T, int H, const void* proj, int E, int topk,
                         const float* per_expert_scale, int norm, int* ids, float* weights, float* partial,
-                        cudaStream_t s) {
+                        cudaStream_t s, int* hist = nullptr, int* lrank = nullptr) {
     CUtensorMap ma, mb;
     int st = make_kmajor_map(&ma, x, T, (long long)H * 2, RouterCfg::BM);
     if (st) return st;
@@ -1311,12 +1407,16 @@ static int route_launch(const void* x, int T, int H, const void* proj, int E, in
     const int tiles = sc.m_tiles * sc.n_tiles * sc.splits;
     st = launch_core<RouterCfg>(ma, mb, cp, sc, e, tiles < sm_count() ? tiles : sm_count(), s);
     if (st) return st;
-    const unsigned blocks = (unsigned)((T + 7) / 8);
     const uint16_t* xn = norm ? static_cast<const uint16_t*>(x) : nullptr;
     const int epl = E / 32;
-#define NVFP4B_TOPK(EPL)                                                                                     \
-    router_topk_kernel<EPL><<<blocks, 256, 0, s>>>(partial, splits, (long long)T * E, T, E, topk, xn, H, \
-                                                   per_expert_scale, ids, weights)
+    const long long stride = (long long)T * E;
+    const int tpw = router_topk_tpw(T, topk, sm_count());
+    const unsigned blocks = hist ? (unsigned)((T + 8 * tpw - 1) / (8 * tpw)) : (unsigned)((T + 7) / 8);
+#define NVFP4B_TOPK(EPL)                                                                                          \
+    st = hist ? launch_k(router_topk_rank_kernel<EPL>, dim3(blocks), dim3(256), 0, s, (const float*)partial,       \
+                         splits, stride, T, E, topk, xn, H, per_expert_scale, ids, weights, hist, lrank, tpw)     \
+              : launch_k(router_topk_kernel<EPL>, dim3(blocks), dim3(256), 0, s, (const float*)partial, splits,    \
+                         stride, T, E, topk, xn, H, per_expert_scale, ids, weights)
     switch (epl) {
         case 1: NVFP4B_TOPK(1); break;
         case 2: NVFP4B_TOPK(2); break;
@@ -1328,7 +1428,7 @@ static int route_launch(const void* x, int T, int H, const void* proj, int E, in
         default: NVFP4B_TOPK(8); break;
     }
 #undef NVFP4B_TOPK
-    return launch_status();
+    return st;
 }
 
 static int route_checks(const void* x, int T, int H, const void* proj, int E, int topk, const int* ids,
@@ -1452,6 +1552,35 @@ extern "C" int nvfp4b_moe_forward_chain(const void* x, int T, const int* ids, co
     if (!x_next || !d_amax_next) return NVFP4B_ERR_NULL;
     return moe_forward(x, T, ids, weights, topk, ex, in_gscale, d_in_amax, out, flags, workspace,
                        CombineNext{static_cast<uint16_t*>(x_next), d_amax_next}, stream);
+}
+
+// Router + layer in one call (the router fused into the MoE prologue): router GEMM, top-k with the dispatch ranking
+// in the same kernel, plan, quantise-scatter, gate/up, down, combine -- seven launches.
+extern "C" int nvfp4b_moe_layer(const void* x, int T, const void* proj, int topk, const float* per_expert_scale,
+                                int norm, const nvfp4b_moe_experts* ex, float in_gscale, const float* d_in_amax,
+                                float* out, int flags, int* ids, float* weights, void* workspace, void* x_next,
+                                float* d_amax_next, void* stream) {
+    if (!proj) return NVFP4B_ERR_NULL;
+    int st = moe_common_checks(x, T, ids, weights, topk, ex, workspace);
+    if (st) return st;
+    const int H = ex->hidden, E = ex->num_experts;
+    st = route_checks(x, T, H, proj, E, topk, ids, weights);
+    if (st) return st;
+    if (!out) return NVFP4B_ERR_NULL;
+    if ((x_next == nullptr) != (d_amax_next == nullptr)) return NVFP4B_ERR_NULL;
+    if (!aligned16(out) || (x_next && !aligned16(x_next))) return NVFP4B_ERR_ALIGN;
+    if (x_next && (flags & NVFP4B_MOE_ATOMIC)) return NVFP4B_ERR_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    const Workspace w = carve(workspace, T, H, ex->inter, E, topk);
+    st = route_launch(x, T, H, proj, E, topk, per_expert_scale, norm, ids, weights, w.partial, s, w.hist, w.lrank);
+    if (st) return st;
+    st = dispatch(x, T, ids, weights, topk, H, E, in_gscale, d_in_amax, w, s, nullptr, 0.f, true,
+                  8 * router_topk_tpw(T, topk, sm_count()) * topk);
+    if (st) return st;
+    st = gate_up<false>(ex, T, topk, in_gscale, d_in_amax, nullptr, w, s);
+    if (st) return st;
+    return down(ex, T, topk, weights, out, flags, w, s, nullptr,
+                CombineNext{static_cast<uint16_t*>(x_next), d_amax_next});
 }
 
 extern "C" int nvfp4b_moe_dispatch(const void* x, int T, const int* ids, const float* weights, int topk,

@@ -222,6 +222,15 @@ class LocalOps:
         return self.pkg.moe_forward(x, ids, weights, self.experts, self.src_ws, in_gscale=in_gscale, in_amax=in_amax,
                                     out=out, accumulate=accumulate, x_next=x_next, amax_next=amax_next)
 
+    def routed_layer(self, x, proj, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False,
+                     x_next=None, amax_next=None):
+        """Router and layer in one call (nvfp4b_moe_layer: the top-k fused with the dispatch ranking)."""
+        if x.shape[0] > self.T_cap:
+            raise ValueError(f"{x.shape[0]} tokens exceed the capacity {self.T_cap}")
+        return self.pkg.moe_layer(x, proj, self.topk, self.experts, self.src_ws, ids=ids, weights=weights,
+                                  in_gscale=in_gscale, in_amax=in_amax, out=out, accumulate=accumulate,
+                                  x_next=x_next, amax_next=amax_next)
+
 
 class ExpertParallelMoE:
     """Runs layers through `ops` over `group` (None = the default group; world size 1 runs with no collective)."""
@@ -278,6 +287,24 @@ class ExpertParallelMoE:
             x_next.copy_(out)
             ops.pkg.amax(x_next, out=amax_next)
         return out
+
+    def forward_routed(self, x, proj, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False,
+                       mark=None, x_next=None, amax_next=None):
+        """Router (x @ proj^T, softmax top-k into ids / weights) and the layer.  One GPU holding every expert runs the
+        fused nvfp4b_moe_layer; the expert-parallel paths route locally and then exchange.  `mark` brackets the
+        timed part as in forward() (the whole layer with its router on one GPU)."""
+        ops = self.ops
+        if getattr(ops, "local", False):
+            if mark is not None:
+                mark("kernel")
+            ops.routed_layer(x, proj, ids, weights, out, in_gscale=in_gscale, in_amax=in_amax,
+                             accumulate=accumulate, x_next=x_next, amax_next=amax_next)
+            if mark is not None:
+                mark("kernel_end")
+            return out
+        ops.pkg.moe_route(x, proj, ops.topk, ops.src_ws, ids=ids, weights=weights)
+        return self.forward(x, ids, weights, out, in_gscale=in_gscale, in_amax=in_amax, accumulate=accumulate,
+                            mark=mark, x_next=x_next, amax_next=amax_next)
 
     def overflowed(self, reset: bool = True) -> bool:
         """True if a layer since the last reset had more than `capacity` records for one rank pair (host read)."""

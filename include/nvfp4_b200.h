@@ -214,6 +214,19 @@ int nvfp4b_moe_forward_chain(const void* x, int T, const int* ids, const float* 
                              const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
                              int flags, void* workspace, void* x_next, float* d_amax_next, void* stream);
 
+/* The router fused into the MoE prologue: nvfp4b_moe_route followed by nvfp4b_moe_forward (x_next, d_amax_next
+ * NULL) or nvfp4b_moe_forward_chain (both given), with the same results, in one call of seven kernel launches: the
+ * router GEMM, the top-k with the dispatch's per-chunk ranking in the same kernel, the segment plan, the quantise-
+ * scatter, the grouped gate/up and down GEMMs and the combine (the chained amax is reset inside the down GEMM, no
+ * memset).  The router is over all experts->num_experts experts (proj [E, H] bf16; per_expert_scale and norm as for
+ * nvfp4b_moe_route); ids [T, topk] int32 and weights [T, topk] fp32 receive the routing.  Replaces the reference's
+ * k_router_hn/scores/top8 + moe() sequence (src/forward.cu:193-231, :516-553).  workspace:
+ * nvfp4b_moe_workspace_bytes(T, H, I, E, topk). */
+int nvfp4b_moe_layer(const void* x, int T, const void* proj, int topk, const float* per_expert_scale, int norm,
+                     const nvfp4b_moe_experts* experts, float in_gscale, const float* d_in_amax, float* out,
+                     int flags, int* ids, float* weights, void* workspace, void* x_next, float* d_amax_next,
+                     void* stream);
+
 /* The three stages of nvfp4b_moe_forward, callable one by one (same stream, same workspace, in this order):
  * dispatch (plan + quantise-scatter of x), gate/up grouped GEMM (writes the NVFP4 intermediate), down grouped GEMM
  * + weighted combine into out (flags as for nvfp4b_moe_forward). */
