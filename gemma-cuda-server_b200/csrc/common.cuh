@@ -336,4 +336,43 @@ __device__ __forceinline__ uint32_t quantize16_bf16(const uint32_t (&w)[8], floa
     return b;
 }
 
+// The straight-line part of quantize16_bf16: the block scale and codes from the fp32 brackets only, no exact paths.
+// Returns the scale byte, with bit 8 set when the result is not proven to be the reference's (the two block-scale
+// brackets or the two code brackets of some element disagree); such a block must be redone by quantize16_bf16.
+__device__ __forceinline__ uint32_t quantize16_bf16_fast(const uint32_t (&w)[8], float g, uint32_t& c0,
+                                                         uint32_t& c1) {
+    float f[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        f[2 * i] = bf16lo(w[i]);
+        f[2 * i + 1] = bf16hi(w[i]);
+    }
+    float bamax = fabsf(f[0]);
+#pragma unroll
+    for (int i = 1; i < 16; ++i) bamax = fmaxf(bamax, fabsf(f[i]));
+    const float t = __fmul_rn(__fmul_rn(g, bamax), 0.16666667163372039795f);
+    const uint32_t two = cvt_e4m3x2(__fmul_rn(t, 1.00000095367431640625f), __fmul_rn(t, 0.99999904632568359375f));
+    uint32_t b = two & 0xFFu;
+    const uint32_t flag = b != (two >> 8) ? 0x100u : 0u;
+    if (b == 0u) b = 0x80u;                       // a zero scale is stored as 0x80 (reference quirk)
+    const float stored = (b & 0x7Fu) ? e4m3_value(b & 0x7Fu) : 0.0f;
+    const float invL = (b & 0x7Fu) ? __fmul_rn(g, rcp_approx(stored)) : 1.0f;
+    const float2 ml = make_float2(invL * 0.99999904632568359375f, invL * 0.99999904632568359375f);
+    const float2 mh = make_float2(invL * 1.00000095367431640625f, invL * 1.00000095367431640625f);
+    float lo[16], hi[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float2 x2 = make_float2(f[2 * i], f[2 * i + 1]);
+        const float2 l = __ffma2_rn(x2, ml, make_float2(0.f, 0.f));
+        const float2 h = __ffma2_rn(x2, mh, make_float2(0.f, 0.f));
+        lo[2 * i] = l.x; lo[2 * i + 1] = l.y;
+        hi[2 * i] = h.x; hi[2 * i + 1] = h.y;
+    }
+    const uint32_t l0 = cvt_e2m1x8(lo[0], lo[1], lo[2], lo[3], lo[4], lo[5], lo[6], lo[7]);
+    const uint32_t l1 = cvt_e2m1x8(lo[8], lo[9], lo[10], lo[11], lo[12], lo[13], lo[14], lo[15]);
+    c0 = cvt_e2m1x8(hi[0], hi[1], hi[2], hi[3], hi[4], hi[5], hi[6], hi[7]);
+    c1 = cvt_e2m1x8(hi[8], hi[9], hi[10], hi[11], hi[12], hi[13], hi[14], hi[15]);
+    return b | flag | ((((l0 ^ c0) | (l1 ^ c1)) != 0u) ? 0x100u : 0u);
+}
+
 }  // namespace nvfp4b
