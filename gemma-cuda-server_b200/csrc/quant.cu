@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(256) quantize_kernel(const T* __restrict__ x, 
 // path of one lane at every step.  The redo overwrites the block's codes and scale (the warp barrier orders the two
 // stores).
 constexpr int kQuantRowsBlock = 256;
-constexpr int kFixSteps = 16;     // steps whose flags one 32-bit lane mask holds (2 blocks per step)
+constexpr int kQuantBPL = 2;                  // blocks per lane per step: a warp-step covers 32 * kQuantBPL blocks
+constexpr int kFixSteps = 32 / kQuantBPL;     // steps whose flags one 32-bit lane mask holds
 
 __global__ void __launch_bounds__(kQuantRowsBlock, 4) quantize_bf16_rows_kernel(const uint16_t* __restrict__ x, int M,
                                                                              int K, float gscale,
@@ -110,54 +111,47 @@ __global__ void __launch_bounds__(kQuantRowsBlock, 4) quantize_bf16_rows_kernel(
                                                                              uint8_t* __restrict__ packed,
                                                                              uint8_t* __restrict__ scales,
                                                                              int tile_cols, int rows_padded) {
-    __shared__ int fix_list[kQuantRowsBlock / 32][32 * 2 * kFixSteps];
+    __shared__ int fix_list[kQuantRowsBlock / 32][32 * 32];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int warps = (int)((gridDim.x * blockDim.x) >> 5);
     const float g = d_amax ? gscale_from_amax(__ldg(d_amax)) : gscale;
     const int kb = K >> 4, bmax = tile_cols * 4;
+    constexpr int kStep = 32 * kQuantBPL;
     int* list = fix_list[wid];
     for (int m = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); m < rows_padded; m += warps) {
         const bool real = m < M;
         const uint16_t* xr = x + (size_t)(real ? m : 0) * K;
         uint8_t* pr = packed + (size_t)(real ? m : 0) * (K >> 1);
         uint8_t* sr = scales + (size_t)(m >> 7) * tile_cols * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4;
-        for (int s0 = 0; s0 < bmax; s0 += 64 * kFixSteps) {
-            uint32_t mask = 0;     // bit 2i (+1): block a (b) of step i needs the exact path
-            const int s1 = min(bmax, s0 + 64 * kFixSteps);
-            for (int b0 = s0; b0 < s1; b0 += 64) {
-                const int ba = b0 + lane, bb = ba + 32;
-                const bool va = real && ba < kb, vb = real && bb < kb;
-                uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, c0 = a0, c1 = a0;
-                if (va) {
-                    a0 = __ldg(reinterpret_cast<const uint4*>(xr + ba * 16));
-                    a1 = __ldg(reinterpret_cast<const uint4*>(xr + ba * 16) + 1);
-                }
-                if (vb) {
-                    c0 = __ldg(reinterpret_cast<const uint4*>(xr + bb * 16));
-                    c1 = __ldg(reinterpret_cast<const uint4*>(xr + bb * 16) + 1);
-                }
-                const int step = (b0 - s0) >> 6;
-                if (ba < bmax) {
-                    uint32_t sf = 0;
-                    if (va) {
-                        const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                        uint32_t q0, q1;
-                        sf = quantize16_bf16_fast(w, g, q0, q1);
-                        *reinterpret_cast<uint2*>(pr + ba * 8) = make_uint2(q0, q1);
-                        mask |= (sf >> 8) << (2 * step);
+        for (int s0 = 0; s0 < bmax; s0 += kStep * kFixSteps) {
+            uint32_t mask = 0;     // bit kQuantBPL * i + j: block j of step i needs the exact path
+            const int s1 = min(bmax, s0 + kStep * kFixSteps);
+            for (int b0 = s0; b0 < s1; b0 += kStep) {
+                uint4 q[kQuantBPL][2];
+#pragma unroll
+                for (int j = 0; j < kQuantBPL; ++j) {       // every load of the step before any encode
+                    const int b = b0 + lane + 32 * j;
+                    q[j][0] = q[j][1] = make_uint4(0, 0, 0, 0);
+                    if (real && b < kb) {
+                        q[j][0] = __ldg(reinterpret_cast<const uint4*>(xr + b * 16));
+                        q[j][1] = __ldg(reinterpret_cast<const uint4*>(xr + b * 16) + 1);
                     }
-                    sr[(ba >> 2) * 512 + (ba & 3)] = (uint8_t)sf;
                 }
-                if (bb < bmax) {
+                const int step = (b0 - s0) / kStep;
+#pragma unroll
+                for (int j = 0; j < kQuantBPL; ++j) {
+                    const int b = b0 + lane + 32 * j;
+                    if (b >= bmax) continue;
                     uint32_t sf = 0;
-                    if (vb) {
-                        const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                        uint32_t q0, q1;
-                        sf = quantize16_bf16_fast(w, g, q0, q1);
-                        *reinterpret_cast<uint2*>(pr + bb * 8) = make_uint2(q0, q1);
-                        mask |= (sf >> 8) << (2 * step + 1);
+                    if (real && b < kb) {
+                        const uint32_t w[8] = {q[j][0].x, q[j][0].y, q[j][0].z, q[j][0].w,
+                                               q[j][1].x, q[j][1].y, q[j][1].z, q[j][1].w};
+                        uint32_t k0, k1;
+                        sf = quantize16_bf16_fast(w, g, k0, k1);
+                        *reinterpret_cast<uint2*>(pr + b * 8) = make_uint2(k0, k1);
+                        mask |= (sf >> 8) << (kQuantBPL * step + j);
                     }
-                    sr[(bb >> 2) * 512 + (bb & 3)] = (uint8_t)sf;
+                    sr[(b >> 2) * 512 + (b & 3)] = (uint8_t)sf;
                 }
             }
             // cooperative exact redo of the noted blocks of these steps
@@ -174,7 +168,7 @@ __global__ void __launch_bounds__(kQuantRowsBlock, 4) quantize_bf16_rows_kernel(
             while (mask) {
                 const int bit = __ffs(mask) - 1;
                 mask &= mask - 1;
-                list[pos++] = s0 + (bit >> 1) * 64 + lane + (bit & 1) * 32;
+                list[pos++] = s0 + (bit / kQuantBPL) * kStep + lane + (bit % kQuantBPL) * 32;
             }
             __syncwarp();
             for (int i = lane; i < total; i += 32) {
