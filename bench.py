@@ -617,14 +617,16 @@ class EpWorkload:
         self.kernel_name = ("one MoE layer with its router (nvfp4b_moe_layer: router GEMM, top-k + dispatch ranking, "
                             "plan, quantise-scatter, grouped gate/up and down GEMMs, combine)"
                             if exchange == "local" else
-                            "expert side of one layer (record scatter, grouped gate/up and down GEMMs, rows stored "
-                            "back), including its wait for the other ranks' records")
+                            "one expert-parallel layer on this rank with its router (nvfp4b_ep_p2p_layer: route, "
+                            "records stored to the peers, local experts, rows stored back, combine), including its "
+                            "waits for the other ranks" if exchange == "p2p" else
+                            "expert side of one layer (record scatter, grouped gate/up and down GEMMs)")
         self.traffic_key = "ep" if exchange == "local" else None
         # one amax, then per layer -- local (nvfp4b_moe_layer): router GEMM, top-k + chunk ranking, plan,
-        # quantise-scatter, gate/up, down, combine; p2p: router x2, hist-rank, plan, pack, then meta, hist-rank, plan,
-        # scatter, gate/up, down, and the combine with the next input fused; nccl: the same plus the amax of the next
-        # input (its combine has no fused output)
-        self.launches_per_step = {"local": 7, "p2p": 12, "nccl": 13}[exchange] * L + 1
+        # quantise-scatter, gate/up, down, combine; p2p (nvfp4b_ep_p2p_layer): router GEMM, top-k + chunk ranking,
+        # plan, pack, then meta + chunk ranking, plan, scatter, gate/up, down, and the combine with the next input
+        # fused; nccl: router x2, hist-rank, plan, pack, meta + ranking, plan, scatter, gate/up, down, combine, amax
+        self.launches_per_step = {"local": 7, "p2p": 10, "nccl": 12}[exchange] * L + 1
         self.kernel_flops = 2.0 * T * topk * 3 * I * H            # expert GEMMs of one layer at even routing
         self.step_flops = L * (2.0 * T * topk * 3 * I * H + 2.0 * T * E * H)
         self.config = {"workload": "cfg4 expert-parallel MoE stack", "layers": L, "rows_total": T * world,
@@ -686,13 +688,17 @@ class EpWorkload:
         """Algorithmic DRAM bytes of the timed part of one layer: the NVFP4 weights (codes + tile scales) of every
         local expert that received a row, read once, plus the layer's activations -- local layer (router included):
         x in (bf16), the residual read and written (fp32), the next input out (bf16) and the bf16 router weights;
-        expert side of a rank: the records in (one per assignment) and one fp16 row per record out."""
+        expert side of a rank: the records in (one per assignment) and one fp16 row per record out; the fused
+        peer-memory layer runs both sides on every rank, so it counts both."""
         counts = self._rows_per_expert()
         hit = sum(1 for c in counts if c > 0)
         n = sum(counts)
         w = hit * self._expert_bytes()
         if self.exchange == "local":
             act = self.T * self.H * (2 + 4 + 4 + 2) + self.E * self.H * 2     # + the bf16 router weights
+        elif self.exchange == "p2p":   # the whole layer on this rank: its tokens' side and its experts' side
+            act = (self.T * self.H * (2 + 4 + 4 + 2) + self.E * self.H * 2 +
+                   n * (self.pkg.ep_record_bytes(self.H) + 2 * self.H))
         else:
             act = n * (self.pkg.ep_record_bytes(self.H) + 2 * self.H)
         return {"weights": w, "activations": act, "total": w + act, "experts_hit": hit, "rows": n}

@@ -558,6 +558,9 @@ def _p2p_sigs():
         "nvfp4b_ep_p2p_combine_chain": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, PP, _P,
                                          ctypes.c_int, _P, _P, _P], ctypes.c_int),
         "nvfp4b_ep_set_peer_wait_ns": ([ctypes.c_ulonglong], ctypes.c_int),
+        "nvfp4b_ep_p2p_layer": ([_P, ctypes.c_int, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int,
+                                 ctypes.POINTER(_Experts), ctypes.c_float, _P, _P, ctypes.c_int, _P, _P, _P, _P, PP,
+                                 _P, _P, _P, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_state": ([PP, _P], ctypes.c_int),
         "nvfp4b_ep_p2p_recv_counts": ([PP, _P], ctypes.c_int),
         "nvfp4b_ipc_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
@@ -648,6 +651,21 @@ def ep_p2p_expert_forward(experts: MoeExperts, workspace, peers: EpPeers, stream
     ex = experts.struct()
     _check("ep_p2p_expert_forward", _p2p_sigs().nvfp4b_ep_p2p_expert_forward(
         ctypes.byref(ex), _ptr(workspace), ctypes.byref(peers), _stream(stream)))
+
+
+def ep_p2p_layer(x, proj, topk: int, E: int, experts: MoeExperts, src_ws, exp_ws, peers: EpPeers, overflow, ids,
+                 weights, out, accumulate: bool = False, in_gscale: float | None = None, in_amax=None,
+                 per_expert_scale=None, norm: bool = False, x_next=None, amax_next=None, stream=None):
+    """Router + one expert-parallel layer on this rank (nvfp4b_ep_p2p_layer): route, dispatch over peer memory, the
+    local experts, combine (+ the chained next input and amax)."""
+    T = x.shape[0]
+    ex = experts.struct()
+    _check("ep_p2p_layer", _p2p_sigs().nvfp4b_ep_p2p_layer(
+        _ptr(x), T, _ptr(proj), topk, _ptr(per_expert_scale), 1 if norm else 0, E, ctypes.byref(ex),
+        float(in_gscale or 0.0), _ptr(in_amax), _ptr(out), MOE_ACCUMULATE if accumulate else 0, _ptr(ids),
+        _ptr(weights), _ptr(src_ws), _ptr(exp_ws), ctypes.byref(peers), _ptr(overflow), _ptr(x_next),
+        _ptr(amax_next), _stream(stream)))
+    return out
 
 
 def ep_p2p_combine(T: int, topk: int, E: int, workspace, peers: EpPeers, out, accumulate: bool = False,

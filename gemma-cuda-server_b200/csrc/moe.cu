@@ -923,7 +923,7 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(const int* __restrict__ hi
 // Warp per token: quantise x[t] once (dynamic or static global scale), write one record per routed slot.
 // kPackWarps warps per token, each quantising every kPackWarps-th run of 32 blocks of x[t] and writing them to all
 // of the token's records.  slot[a] = d * capacity + (pos - dst_start[d]) for the assignment's destination d, where
-// pos = chunk_base[a / kChunk][e] + lrank[a] is its compact expert-sorted position, or -1 past the capacity
+// pos = chunk_base[a / chunk][e] + lrank[a] is its compact expert-sorted position, or -1 past the capacity
 // (overflowed, not sent).  The record goes to
 // records[slot], or with peers.recv to peer d's receive slot rank * capacity + (slot - d * capacity); the last
 // block then stores the per-destination counts, raises the records-landed flags and advances the layer epoch.
@@ -931,7 +931,7 @@ constexpr int kPackWarps = 6;
 
 __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict__ x, int T, int H, int topk,
                                                       const int* __restrict__ chunk_base,
-                                                      const int* __restrict__ lrank, int E,
+                                                      const int* __restrict__ lrank, int chunk, int E,
                                                       const int* __restrict__ ids,
                                                       const float* __restrict__ weights, int experts_per_rank,
                                                       int capacity, const int* __restrict__ dst_start,
@@ -948,7 +948,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
         if (lane < topk) {
             const long long a = (long long)t * topk + lane;
             const int e = __ldg(ids + a), r = __ldg(lrank + a);
-            const int pos = (e >= 0 && e < E && r >= 0) ? __ldg(chunk_base + (a / kChunk) * E + e) + r : -1;
+            const int pos = (e >= 0 && e < E && r >= 0) ? __ldg(chunk_base + (a / chunk) * E + e) + r : -1;
             int my_slot = -1;
             if (pos >= 0) {
                 const int d = __ldg(ids + a) / experts_per_rank;
@@ -1004,22 +1004,31 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint16_t* __restrict
 
 // Slot i = s * capacity + j holds a record iff j < recv_counts[s]; empty slots get expert -1 (skipped by the plan).
 // With wait_flags (exchange over peer memory) every block first waits for the records-landed flags of this layer.
-__global__ void __launch_bounds__(256) ep_meta_kernel(const uint8_t* records, int n, int H, int capacity,
-                                                      const int* recv_counts, int* __restrict__ ids,
-                                                      float* __restrict__ w, const unsigned* wait_flags, int G,
-                                                      const unsigned* state, int* err,
-                                                      unsigned long long wait_ns) {
+// One block per chunk of kChunk slots: each thread reads its slot's meta, then the block ranks its chunk for the
+// dispatch plan (chunk_hist_rank) -- the meta read and the ranking in one launch.
+__global__ void __launch_bounds__(256) ep_meta_rank_kernel(const uint8_t* records, int n, int H, int capacity,
+                                                           const int* recv_counts, int* __restrict__ ids,
+                                                           float* __restrict__ w, int E, int* __restrict__ hist,
+                                                           int* __restrict__ lrank, const unsigned* wait_flags, int G,
+                                                           const unsigned* state, int* err,
+                                                           unsigned long long wait_ns) {
+    static_assert(kChunk == 256, "one slot per thread");
     if (wait_flags) wait_peer_flags(wait_flags, G, state[kEpEpoch], err, wait_ns);
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    if (i % capacity >= recv_counts[i / capacity]) {
-        ids[i] = -1;
-        w[i] = 0.f;
-        return;
+    const int i = blockIdx.x * kChunk + threadIdx.x;
+    const bool valid = i < n;
+    int e = -1;
+    if (valid) {
+        float wt = 0.f;
+        if (i % capacity < recv_counts[i / capacity]) {
+            const EpMeta meta =
+                *reinterpret_cast<const EpMeta*>(records + (size_t)i * ep_record_bytes(H) + (H / 2) + (H / 16));
+            e = meta.expert;
+            wt = meta.weight;
+        }
+        ids[i] = e;
+        w[i] = wt;
     }
-    const EpMeta meta = *reinterpret_cast<const EpMeta*>(records + (size_t)i * ep_record_bytes(H) + (H / 2) + (H / 16));
-    ids[i] = meta.expert;
-    w[i] = meta.weight;
+    chunk_hist_rank(e, i, valid, E, blockIdx.x, hist, lrank);
 }
 
 // Warp per received record slot i: its row r = chunk_base[i / kChunk][e] + lrank[i] of the padded expert-sorted
@@ -1179,7 +1188,7 @@ int gate_up(const nvfp4b_moe_experts* ex, int T, int topk, float in_gscale, cons
 
 int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, float* out, int flags,
          const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr,
-         const CombineNext next = CombineNext{nullptr, nullptr}) {
+         const CombineNext next = CombineNext{nullptr, nullptr}, float* zero_word = nullptr) {
     const bool accumulate = (flags & NVFP4B_MOE_ACCUMULATE) != 0;
     const bool deterministic = (flags & NVFP4B_MOE_ATOMIC) == 0;
     const int H = ex->hidden, I = ex->inter, E = ex->num_experts;
@@ -1218,7 +1227,7 @@ int down(const nvfp4b_moe_experts* ex, int T, int topk, const float* weights, fl
         e.transpose = peers != nullptr || (long long)T * topk >= kDownTransposeRows;
         // the chained amax is zeroed by the down kernel: every reader of the layer's input scale (the dispatch and
         // the gate/up epilogue) has finished by then, and the combine that accumulates it runs after
-        e.zero_word = (out && next.x) ? next.amax : nullptr;
+        e.zero_word = (out && next.x) ? next.amax : zero_word;
         static_assert(DownTransposeCfg::BM == DownCfg::BM && DownTransposeCfg::BN == DownCfg::BN, "same tiles, maps");
         st = e.transpose ? launch_core<DownTransposeCfg>(ma, mb, cp, sc, e, sm_count(), s)
                          : launch_core<DownCfg>(ma, mb, cp, sc, e, sm_count(), s);
@@ -1247,9 +1256,9 @@ int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weight
     ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, capacity, w.chunk_base, w.seg_count,
                                      w.seg_start, send_counts, overflow);
     ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk,
-                                                            w.chunk_base, w.lrank, E, ids, weights, E / G, capacity,
-                                                            w.seg_start, in_gscale, d_in_amax, records, w.ep_ids,
-                                                            EpPackPeers{});
+                                                            w.chunk_base, w.lrank, kChunk, E, ids, weights, E / G,
+                                                            capacity, w.seg_start, in_gscale, d_in_amax, records,
+                                                            w.ep_ids, EpPackPeers{});
     return launch_status();
 }
 
@@ -1257,11 +1266,11 @@ int ep_dispatch(const void* x, int T, int H, const int* ids, const float* weight
 // ranks' receive slots and the counts + records-landed flags published by the pack kernel.
 int ep_dispatch_p2p(const void* x, int T, int H, const int* ids, const float* weights, int topk, int E,
                     float in_gscale, const float* d_in_amax, const Workspace& w, const nvfp4b_ep_peers& pr,
-                    int* overflow, cudaStream_t s) {
+                    int* overflow, cudaStream_t s, bool ranked = false, int chunk = kChunk) {
     const int G = pr.G, capacity = pr.capacity;
     const int n_assign = T * topk;
-    const int n_chunks = (n_assign + kChunk - 1) / kChunk;
-    moe_hist_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist, w.lrank);
+    const int n_chunks = (n_assign + chunk - 1) / chunk;
+    if (!ranked) moe_hist_rank_kernel<<<n_chunks, 256, 0, s>>>(ids, n_assign, E, w.hist, w.lrank);
     ep_plan_kernel<<<1, 256, 0, s>>>(w.hist, n_chunks, E, E / G, G, capacity, w.chunk_base, w.seg_count,
                                      w.seg_start, w.ep_send, overflow);
     EpPackPeers pp;
@@ -1273,25 +1282,26 @@ int ep_dispatch_p2p(const void* x, int T, int H, const int* ids, const float* we
     pp.rank = pr.rank;
     pp.G = G;
     ep_pack_kernel<<<(T * kPackWarps + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x), T, H, topk,
-                                                            w.chunk_base, w.lrank, E, ids, weights, E / G, capacity,
-                                                            w.seg_start, in_gscale, d_in_amax, nullptr, w.ep_ids, pp);
+                                                            w.chunk_base, w.lrank, chunk, E, ids, weights, E / G,
+                                                            capacity, w.seg_start, in_gscale, d_in_amax, nullptr,
+                                                            w.ep_ids, pp);
     return launch_status();
 }
 
 // expert parallelism, expert side: received records -> padded expert-sorted operand -> gate/up -> down GEMM, leaving
 // each record's weighted output row (fp16) in w.y in record order.
 int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_counts, const nvfp4b_moe_experts* ex,
-              const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr) {
+              const Workspace& w, cudaStream_t s, const nvfp4b_ep_peers* peers = nullptr,
+              float* zero_word = nullptr) {
     const int H = ex->hidden, E = ex->num_experts;
     const int n = G * capacity;
     const int n_chunks = (n + kChunk - 1) / kChunk;
     int* err = device_error_ptr();
     if (!err) return NVFP4B_ERR_CUDA;
-    ep_meta_kernel<<<(n + 255) / 256, 256, 0, s>>>(records, n, H, capacity, recv_counts, w.ep_ids, w.ep_w,
-                                                   peers ? peers->my_flags : nullptr, G,
-                                                   peers ? peers->state : nullptr, err,
-                                                   g_peer_wait_ns.load(std::memory_order_relaxed));
-    moe_hist_rank_kernel<<<n_chunks, 256, 0, s>>>(w.ep_ids, n, E, w.hist, w.lrank);
+    ep_meta_rank_kernel<<<n_chunks, 256, 0, s>>>(records, n, H, capacity, recv_counts, w.ep_ids, w.ep_w, E, w.hist,
+                                                  w.lrank, peers ? peers->my_flags : nullptr, G,
+                                                  peers ? peers->state : nullptr, err,
+                                                  g_peer_wait_ns.load(std::memory_order_relaxed));
     moe_plan_kernel<<<1, kPlanThreads, 0, s>>>(w.hist, n_chunks, E, w.chunk_base, w.seg_start, w.seg_count,
                                                w.m_tiles, w.tile_expert);
     const int tile_cols = (H / 16 + 3) / 4;
@@ -1302,7 +1312,7 @@ int ep_expert(const uint8_t* records, int G, int capacity, const int* recv_count
     if (st) return st;
     st = gate_up<false>(ex, n, 1, 1.0f, nullptr, nullptr, w, s, true);
     if (st) return st;
-    return down(ex, n, 1, w.ep_w, nullptr, 0, w, s, peers);
+    return down(ex, n, 1, w.ep_w, nullptr, 0, w, s, peers, CombineNext{nullptr, nullptr}, zero_word);
 }
 
 // Gate/up interleave: w13 row 32g + r <- gate row 16g + r; 32g + 16 + r <- up row 16g + r.
@@ -1752,7 +1762,7 @@ extern "C" int nvfp4b_ep_p2p_expert_forward(const nvfp4b_moe_experts* ex, void* 
 }
 
 static int ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
-                          float* out, int flags, const CombineNext next, void* stream) {
+                          float* out, int flags, const CombineNext next, void* stream, bool amax_zeroed = false) {
     if (!workspace || !out) return NVFP4B_ERR_NULL;
     const int st = check_peers(peers);
     if (st) return st;
@@ -1762,7 +1772,7 @@ static int ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, 
     int* err = device_error_ptr();
     if (!err) return NVFP4B_ERR_CUDA;
     const cudaStream_t s = (cudaStream_t)stream;
-    if (next.x) {
+    if (next.x && !amax_zeroed) {
         const cudaError_t e = cudaMemsetAsync(next.amax, 0, sizeof(float), s);
         if (e != cudaSuccess) return record_cuda_error(e);
     }
@@ -1785,6 +1795,43 @@ extern "C" int nvfp4b_ep_p2p_combine_chain(int T, int H, int topk, int E, const 
     if (!x_next || !d_amax_next) return NVFP4B_ERR_NULL;
     return ep_p2p_combine(T, H, topk, E, workspace, peers, out, flags,
                           CombineNext{static_cast<uint16_t*>(x_next), d_amax_next}, stream);
+}
+
+// Router + one expert-parallel layer on this rank in one call: the router top-k shares its kernel with the
+// dispatch ranking, the chained amax is reset inside the down GEMM (no memset).
+extern "C" int nvfp4b_ep_p2p_layer(const void* x, int T, const void* proj, int topk, const float* per_expert_scale,
+                                   int norm, int E, const nvfp4b_moe_experts* local_experts, float in_gscale,
+                                   const float* d_in_amax, float* out, int flags, int* ids, float* weights,
+                                   void* src_workspace, void* exp_workspace, const nvfp4b_ep_peers* peers,
+                                   int* overflow, void* x_next, float* d_amax_next, void* stream) {
+    if (!x || !proj || !ids || !weights || !src_workspace || !exp_workspace || !overflow || !out)
+        return NVFP4B_ERR_NULL;
+    if ((x_next == nullptr) != (d_amax_next == nullptr)) return NVFP4B_ERR_NULL;
+    int st = check_experts(local_experts);
+    if (st) return st;
+    st = check_peers(peers);
+    if (st) return st;
+    const int G = peers->G, H = local_experts->hidden;
+    if (local_experts->num_experts * G != E) return NVFP4B_ERR_SHAPE;
+    st = route_checks(x, T, H, proj, E, topk, ids, weights);
+    if (st) return st;
+    if (flags & ~NVFP4B_MOE_ACCUMULATE) return NVFP4B_ERR_ARG;
+    if (!aligned16(src_workspace) || !aligned16(exp_workspace) || !aligned16(out) || (x_next && !aligned16(x_next)))
+        return NVFP4B_ERR_ALIGN;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const Workspace ws = carve(src_workspace, T, H, 32, E, topk);
+    st = route_launch(x, T, H, proj, E, topk, per_expert_scale, norm, ids, weights, ws.partial, s, ws.hist, ws.lrank);
+    if (st) return st;
+    st = ep_dispatch_p2p(x, T, H, ids, weights, topk, E, in_gscale, d_in_amax, ws, *peers, overflow, s, true,
+                         8 * router_topk_tpw(T, topk, sm_count()) * topk);
+    if (st) return st;
+    const Workspace we = carve(exp_workspace, G * peers->capacity, H, local_experts->inter,
+                               local_experts->num_experts, 1);
+    // the pack kernel above was the last reader of this layer's input scale on this rank
+    st = ep_expert(peers->my_recv, G, peers->capacity, peers->my_counts, local_experts, we, s, peers, d_amax_next);
+    if (st) return st;
+    return ep_p2p_combine(T, H, topk, E, src_workspace, peers, out, flags,
+                          CombineNext{static_cast<uint16_t*>(x_next), d_amax_next}, stream, true);
 }
 
 extern "C" int nvfp4b_ep_set_peer_wait_ns(unsigned long long ns) {

@@ -199,6 +199,16 @@ class P2PKernelOps:
         return self.pkg.ep_p2p_combine(self.T, self.topk, self.E, self.src_ws, self.ex.peers, out,
                                        accumulate=accumulate, x_next=x_next, amax_next=amax_next)
 
+    def routed_layer(self, x, proj, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False,
+                     x_next=None, amax_next=None):
+        """Router and the whole layer on this rank in one call (nvfp4b_ep_p2p_layer)."""
+        if x.shape[0] > self.T_cap:
+            raise ValueError(f"{x.shape[0]} tokens exceed the capacity {self.T_cap}")
+        self.T = x.shape[0]
+        return self.pkg.ep_p2p_layer(x, proj, self.topk, self.E, self.experts, self.src_ws, self.exp_ws,
+                                     self.ex.peers, self.overflow, ids, weights, out, accumulate=accumulate,
+                                     in_gscale=in_gscale, in_amax=in_amax, x_next=x_next, amax_next=amax_next)
+
 
 class LocalOps:
     """One GPU holding every expert: the layer is the single-GPU MoE (nvfp4b_moe_forward: dispatch with the
@@ -291,10 +301,10 @@ class ExpertParallelMoE:
     def forward_routed(self, x, proj, ids, weights, out, in_gscale=None, in_amax=None, accumulate: bool = False,
                        mark=None, x_next=None, amax_next=None):
         """Router (x @ proj^T, softmax top-k into ids / weights) and the layer.  One GPU holding every expert runs the
-        fused nvfp4b_moe_layer; the expert-parallel paths route locally and then exchange.  `mark` brackets the
-        timed part as in forward() (the whole layer with its router on one GPU)."""
+        fused nvfp4b_moe_layer, the peer-memory path the fused nvfp4b_ep_p2p_layer; the NCCL path routes and then
+        exchanges.  `mark` brackets the timed part (the whole layer with its router for the fused forms)."""
         ops = self.ops
-        if getattr(ops, "local", False):
+        if getattr(ops, "local", False) or getattr(ops, "p2p", False):
             if mark is not None:
                 mark("kernel")
             ops.routed_layer(x, proj, ids, weights, out, in_gscale=in_gscale, in_amax=in_amax,

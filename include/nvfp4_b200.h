@@ -365,6 +365,17 @@ int nvfp4b_ep_p2p_combine(int T, int H, int topk, int E, const void* workspace, 
 int nvfp4b_ep_p2p_combine_chain(int T, int H, int topk, int E, const void* workspace, const nvfp4b_ep_peers* peers,
                                 float* out, int flags, void* x_next, float* d_amax_next, void* stream);
 
+/* Router + one expert-parallel layer on this rank in one call: nvfp4b_moe_route over all E experts (proj [E, H]),
+ * nvfp4b_ep_p2p_dispatch, nvfp4b_ep_p2p_expert_forward (local_experts: this rank's E / G) and
+ * nvfp4b_ep_p2p_combine (x_next / d_amax_next NULL) or _combine_chain (both given), with the same results, and with
+ * the router top-k sharing its kernel with the dispatch ranking and the chained amax reset inside the down GEMM (no
+ * memset).  ids / weights [T, topk] receive the routing; src_workspace / exp_workspace as for the dispatch and the
+ * expert side.  flags: NVFP4B_MOE_ACCUMULATE or 0. */
+int nvfp4b_ep_p2p_layer(const void* x, int T, const void* proj, int topk, const float* per_expert_scale, int norm,
+                        int E, const nvfp4b_moe_experts* local_experts, float in_gscale, const float* d_in_amax,
+                        float* out, int flags, int* ids, float* weights, void* src_workspace, void* exp_workspace,
+                        const nvfp4b_ep_peers* peers, int* overflow, void* x_next, float* d_amax_next, void* stream);
+
 /* Bound of every wait on another rank's flag (records landed, rows landed) in kernels launched after this call:
  * ns nanoseconds per flag, 1 us ... 600 s; 0 restores the default of 10 s.  A wait that runs out records
  * NVFP4B_ERR_TIMEOUT's device code (nvfp4b_read_device_error() == 4) and its kernel goes on; the exchange's layer

@@ -1,7 +1,7 @@
 """Expert-parallel MoE over NVLink peer memory on real GPUs: one process per GPU (NCCL process group only for the
 set-up exchange of CUDA IPC handles), each rank owning E/G experts and T tokens.  Every rank's output must equal
 nvfp4b_moe_forward over the full expert arena for its tokens, bit for bit, eagerly and when the layer is replayed
-from a CUDA graph.  Needs at least 2 GPUs (skipped otherwise)."""
+from a CUDA graph; the router-fused form (nvfp4b_ep_p2p_layer) must equal nvfp4b_moe_layer likewise.  Needs at least 2 GPUs (skipped otherwise)."""
 import os
 import socket
 
@@ -60,6 +60,19 @@ def _worker(rank, world, port, q):
             g.replay()
             torch.cuda.synchronize()
             results.append(torch.equal(out, ref))
+        # the fused form (nvfp4b_ep_p2p_layer: router + layer on this rank in one call) against the single-GPU
+        # router-fused layer over the full arena, eagerly, twice
+        ids_f = torch.empty((T, TOPK), dtype=torch.int32, device="cuda")
+        w_f = torch.empty((T, TOPK), dtype=torch.float32, device="cuda")
+        ref_ids = torch.empty_like(ids_f)
+        ref_w = torch.empty_like(w_f)
+        ref_f = p.moe_layer(x, P["proj"], TOPK, P["arena"], P["ws"], ids=ref_ids, weights=ref_w, in_amax=amax).clone()
+        for _ in range(2):
+            out.fill_(float("nan"))
+            layer.forward_routed(x, P["proj"], ids_f, w_f, out, in_amax=amax)
+            torch.cuda.synchronize()
+            dist.barrier()
+            results.append(torch.equal(out, ref_f) and torch.equal(ids_f, ref_ids) and torch.equal(w_f, ref_w))
         err = p.read_device_error()
         state = ex.state_words()
         del g
@@ -97,4 +110,4 @@ def test_ep_p2p_processes_bit_identical(world):
         assert err == 0, (r, err)
         assert overflow == 0
         assert all(results), (r, results)
-        assert state[:3] == [5, 0, 0], (r, state)      # 3 eager layers + 2 replays; counters reset
+        assert state[:3] == [7, 0, 0], (r, state)      # 3 eager layers + 2 replays + 2 fused; counters reset
