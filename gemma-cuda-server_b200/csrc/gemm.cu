@@ -276,6 +276,20 @@ int make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long lon
     return r == CUDA_SUCCESS ? NVFP4B_OK : NVFP4B_ERR_ALIGN;
 }
 
+int make_rows_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_bytes,
+                  int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return record_cuda_error(cudaErrorNotSupported);
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? NVFP4B_OK : NVFP4B_ERR_ALIGN;
+}
+
 int make_scale_map(CUtensorMap* map, const void* base, long long bytes) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return record_cuda_error(cudaErrorNotSupported);

@@ -640,6 +640,9 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 // ---------------------------------------------------------------------------------------------------------------
 
 int make_kmajor_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_rows);
+// Row-major byte matrix [rows, row_bytes] (row_bytes a multiple of 16) in boxes of box_bytes x box_rows, no swizzle.
+int make_rows_map(CUtensorMap* map, const void* base, long long rows, long long row_bytes, int box_bytes,
+                  int box_rows);
 // Tile-layout scale buffer of `bytes` (a multiple of 512) as rows of 256 bytes, boxes of 8 rows (2 KB), no swizzle.
 int make_scale_map(CUtensorMap* map, const void* base, long long bytes);
 

@@ -40,8 +40,14 @@ def _check_fp32_accumulation(got, ref, bound):
     assert np.all(d <= lim), f"max err {d.max():.3e}, worst ratio {(d / lim).max():.3f}"
 
 
+# M <= 2 with K % 256 == 0: the TMA-fed kernel ((1, 60000, 256): more 256-row tasks than SMs); M <= 8: the
+# register-fed kernel ((3, 60000, 256): more row groups than resident warps; (6, 129, 2080): K % 64 != 0); larger M
+# with K % 64 == 0: passes of 16 rows through the cp.async ring kernel (M = 37, 130: several passes, the last of
+# <= 8 rows); (12, 50, 2080): the FFMA kernel.
 @pytest.mark.parametrize("M,N,K", [(1, 512, 2816), (5, 300, 2048), (16, 256, 4096), (37, 200, 2816),
-                                   (130, 96, 1024), (1, 1000, 2112)])
+                                   (130, 96, 1024), (1, 1000, 2112), (1, 60000, 256), (2, 4100, 2816),
+                                   (3, 60000, 256), (8, 4100, 2816), (13, 4100, 2816), (6, 129, 2080),
+                                   (12, 50, 2080), (2, 40, 96)])
 def test_w4a16_vs_dequant_oracle(M, N, K):
     p = require_gpu()
     wp, ws, gw, x16 = _operands(M, N, K, seed=M * 7 + N)
