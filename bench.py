@@ -52,7 +52,8 @@ METRIC = "NVFP4 GEMM TFLOPS & quant GB/s vs roofline; MoE tokens/s at 1/2/4/8 B2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum (bytes) of the dominant kernel per launch, from the ncu captures
 # summarised under profiles/ (quantize_bf16_rows_kernel, nvf4_gemm_pair_kernel, the MoE gate/up GEMM).
-NCU_TRAFFIC = {"quant": 46.262272e6, "gemm": 335.105280e6, "moe": 366.175232e6}
+NCU_TRAFFIC = {"quant": 46.262272e6, "gemm": 335.105280e6, "moe": 366.175232e6,
+               "ep": 321.858304e6}   # ep: the layer's dominant kernel, the grouped gate/up GEMM (one launch)
 
 
 def parse_args():
@@ -876,6 +877,36 @@ def run_reference(args, rank, world):
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
+def read_stream_ceiling(pkg, torch, W, flush, stream, barrier, reps=6):
+    """The rate a pure TMA read of layer 0's expert weight codes reaches (nvfp4b_hbm_read_stream: the GEMMs' load
+    path with no compute), one launch per arena as the layer's two grouped GEMMs stream them, L2 flushed before
+    each launch, 3 untimed launches first.  A stream of a few hundred MB runs well below the 1 GiB copy peak (fixed
+    ramp and tail), so this is the ceiling the layer's weight stream is compared with at its own size."""
+    ar = W.layers[0]["arena"]
+    out = {"kernel": "nvfp4b_hbm_read_stream (TMA boxes of 256 rows x 128 B, 4 stages, 1 CTA per SM, no compute)"}
+    total_b, total_s = 0, 0.0
+    for name, t in (("w13_codes", ar.w13), ("w2_codes", ar.w2)):
+        nbytes = t.numel()
+        rows = nbytes // 1408                     # [rows, 1408 B]: H/2 bytes per w13 row, 4 w2 rows (I/2 = 352 B)
+        ms = []
+        for i in range(3 + reps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            pkg.hbm_read_stream(t, rows, 1408)
+            b.record(stream)
+            barrier()
+            if i >= 3:
+                ms.append(a.elapsed_time(b))
+        sec = statistics.median(ms) / 1e3
+        out[name] = {"bytes": rows * 1408, "us": sec * 1e6, "gbs": rows * 1408 / sec / 1e9}
+        total_b += rows * 1408
+        total_s += sec
+    out["gbs"] = total_b / total_s / 1e9
+    out["us"] = total_s * 1e6
+    return out
+
+
 def roofline_of(W, kern_s, peaks, peak_src, steps_s=None):
     """Roofline object of workload W's dominant kernel (or, for ep, one layer), from its event-timed duration."""
     hbm = peaks["hbm_gbs"]
@@ -891,6 +922,8 @@ def roofline_of(W, kern_s, peaks, peak_src, steps_s=None):
         achieved = b["total"] / kern_s / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": NCU_TRAFFIC.get(W.traffic_key), "kernel": W.kernel_name,
+                "traffic_of": "the grouped gate/up GEMM, one launch (ncu dram__bytes_read + write; its algorithmic "
+                              "bytes: 286 MB of w13 codes + scales and 5.8 MB of dispatched rows)",
                 "algorithmic_bytes": b, "layer_us": kern_s * 1e6,
                 "tensor": {"achieved": W.layer_flops() / kern_s / 1e12, "peak": fp4_peak, "unit": "TFLOP/s",
                            "frac": W.layer_flops() / kern_s / 1e12 / fp4_peak},
@@ -1062,6 +1095,8 @@ def main():
     peaks, peak_src = load_peaks()
     kern_s = statistics.mean(kern_ms) / 1e3
     roof = roofline_of(W, kern_s, peaks, peak_src, steps_s=sum(step_ms) / 1e3 / args.steps)
+    if W.name == "ep":
+        roof["read_stream"] = read_stream_ceiling(pkg, torch, W, flush, stream, barrier)
 
     # driver-visible sub-results at N = 1: the quantiser (cfg1) and the dense GEMM (cfg2), same timing rules
     sub = None

@@ -59,6 +59,7 @@ def lib() -> ctypes.CDLL:
             "nvfp4b_gemm": ([_P, _P, ctypes.c_float, _P, _P, _P, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                              ctypes.c_int, _P, ctypes.c_int, ctypes.c_longlong, _P], ctypes.c_int),
             "nvfp4b_read_device_error": ([ctypes.c_int], ctypes.c_int),
+            "nvfp4b_hbm_read_stream": ([_P, ctypes.c_longlong, ctypes.c_int, _P], ctypes.c_int),
             "nvfp4b_gemm_set_tile_config": ([ctypes.c_int], ctypes.c_int),
             "nvfp4b_w4a16_gemm": ([_P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P],
                                   ctypes.c_int),
@@ -223,6 +224,13 @@ def set_gemm_tile_config(config: int) -> None:
 
 def read_device_error(reset: bool = True) -> int:
     return int(lib().nvfp4b_read_device_error(1 if reset else 0))
+
+
+def hbm_read_stream(buf: torch.Tensor, rows: int, row_bytes: int) -> None:
+    """Reads rows x row_bytes bytes of `buf` through the GEMMs' TMA path and discards them (roofline measurement)."""
+    if buf.numel() * buf.element_size() < rows * row_bytes:
+        raise ValueError("hbm_read_stream: buffer smaller than rows * row_bytes")
+    _check("hbm_read_stream", lib().nvfp4b_hbm_read_stream(buf.data_ptr(), rows, row_bytes, _stream()))
 
 
 # ----------------------------------------------------------------------------------------------------------------

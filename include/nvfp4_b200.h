@@ -98,6 +98,12 @@ int nvfp4b_gemm_set_tile_config(int config);
  * Returns 0 if no kernel reported an error. */
 int nvfp4b_read_device_error(int reset);
 
+/* Measurement (no counterpart in the reference): reads a [rows, row_bytes] byte matrix (row_bytes % 128 == 0,
+ * 16-byte aligned) through the TMA path the GEMMs use -- boxes of 256 rows x 128 bytes into a 4-stage shared-memory
+ * ring, one persistent CTA per SM -- and discards it.  bench.py times it at the byte count of a weight-stream-bound
+ * kernel: the ceiling that kernel's stream can reach at its size. */
+int nvfp4b_hbm_read_stream(const void* p, long long rows, int row_bytes, void* stream);
+
 /* ---- W4A16 (replaces fp4_gemv / w4a16_gemm, kernels/fp4_gemm.cu:45-111) ----------------------------------- */
 
 /* out[M, N] (fp32 row-major) = x16[M, K] (fp16 row-major) @ dequant(W[N, K])^T with raw, unswizzled weight codes

@@ -79,6 +79,9 @@ def test_argument_errors_need_no_gpu(built):
     assert L.nvfp4b_quantize_bf16(8, 4, 32, 1.0, None, 16, 16, None) == -2           # misaligned x
     assert L.nvfp4b_gemm(16, 16, 1.0, None, 16, 16, 1.0, 4, 4, 48, 16, 0, 4, None) == -1   # K % 32
     assert L.nvfp4b_gemm(16, 16, 1.0, None, 16, 16, 1.0, 4, 4, 64, 16, 9, 4, None) == -7   # out kind
+    assert L.nvfp4b_hbm_read_stream(None, 256, 1408, None) == -3
+    assert L.nvfp4b_hbm_read_stream(16, 256, 1400, None) == -1                        # row_bytes % 128
+    assert L.nvfp4b_hbm_read_stream(8, 256, 1408, None) == -2                         # misaligned
 
 
 def test_linear_workspace_and_argument_errors_need_no_gpu(built):

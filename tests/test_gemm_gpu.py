@@ -181,3 +181,18 @@ def test_gemm_cfg2_grid_full_size_sampled_rows(M, K, N, cfg):
     assert not torch.isnan(Y).any()                      # every output written (full-size launch)
     ok, msg = gate_w4a4(Y[torch.from_numpy(rows).cuda()].float().cpu().numpy(), ref)
     assert ok, msg
+
+
+def test_hbm_read_stream_measurement_kernel():
+    """nvfp4b_hbm_read_stream (the bench's read ceiling): full and partial 256-row boxes, several boxes per SM; it
+    completes without a device error and leaves its input untouched."""
+    p = require_gpu()
+    buf = torch.randint(0, 256, (3000 * 1408 + 64,), dtype=torch.uint8, device="cuda")
+    before = buf.clone()
+    for rows in (3000, 256, 1, 70000 // 1408 * 10):
+        p.hbm_read_stream(buf, rows, 1408)
+    big = torch.empty(148 * 3 * 256 * 1408, dtype=torch.uint8, device="cuda")
+    p.hbm_read_stream(big, 148 * 3 * 256, 1408)
+    torch.cuda.synchronize()
+    assert p.read_device_error() == 0
+    assert torch.equal(buf, before)
