@@ -73,6 +73,9 @@ def parse_args():
                          "(nccl), the single-GPU MoE layer (local, 1 GPU only), or auto = p2p on 2+ GPUs, local on 1")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--clock-seconds", type=float, default=1.5, help="sustained-load window for clock sampling")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="after the timed steps, two eager steps under torch.profiler (CUPTI activity records): "
+                         "per-kernel device time per step on every rank, to stderr (not a bench value)")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return ap.parse_args()
@@ -877,6 +880,32 @@ def run_reference(args, rank, world):
         "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
+def profile_kernels(torch, W, rank, world, barrier, steps=2):
+    """Per-kernel device time per step of W on this rank (torch.profiler CUDA activity over `steps` eager steps,
+    after the timed ones), printed to stderr rank by rank.  With several ranks a kernel that waits for another rank
+    (record meta, combine) includes its wait."""
+    import collections
+    from torch.profiler import ProfilerActivity, profile
+    barrier()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            W.step()
+        torch.cuda.synchronize()
+    barrier()
+    agg = collections.defaultdict(list)
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            agg[e.name.split("(")[0][:100]].append(e.device_time_total)
+    rows = sorted(agg.items(), key=lambda kv: -sum(kv[1]))
+    total = sum(sum(v) for _, v in rows) / steps
+    text = "\n".join(f"kernels rank {rank}: {len(v) / steps:6.0f}/step {statistics.mean(v):9.2f} us  {k}"
+                      for k, v in rows[:20])
+    for r in range(world):
+        if r == rank:
+            print(text + f"\nkernels rank {rank}: device time per step {total:.1f} us", file=sys.stderr, flush=True)
+        barrier()
+
+
 def read_stream_ceiling(pkg, torch, W, flush, stream, barrier, reps=6):
     """The rate a pure TMA read of layer 0's expert weight codes reaches (nvfp4b_hbm_read_stream: the GEMMs' load
     path with no compute), one launch per arena as the layer's two grouped GEMMs stream them, L2 flushed before
@@ -1091,6 +1120,9 @@ def main():
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_val = W.value(float(te.item()) / n_e2e / 1e3) * world
+
+    if args.profile_kernels:
+        profile_kernels(torch, W, rank, world, barrier)
 
     peaks, peak_src = load_peaks()
     kern_s = statistics.mean(kern_ms) / 1e3
