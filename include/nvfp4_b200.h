@@ -109,7 +109,9 @@ int nvfp4b_hbm_read_stream(const void* p, long long rows, int row_bytes, void* s
 /* out[M, N] (fp32 row-major) = x16[M, K] (fp16 row-major) @ dequant(W[N, K])^T with raw, unswizzled weight codes
  * wp [N, K/2] and e4m3 scales ws [N, K/16]; dequant = code * e4m3 / w_gscale.  K % 16 == 0; any M (the
  * reference's kernel is limited to M <= 16); x16 2-byte aligned.  16-byte aligned operands with K % 32 == 0 take
- * the vectorised path, anything else a byte-granular one. */
+ * the tensor-core paths (TMA-fed for M <= 2 with K % 256 == 0 and 16-byte aligned scales, register-fed for M <= 8,
+ * passes of 16 rows for larger M with K % 64 == 0, each pass reading the weights once), anything else a
+ * byte-granular one.  Sums are fp32 in every path. */
 int nvfp4b_w4a16_gemm(float* out, const uint8_t* wp, const uint8_t* ws, float w_gscale, const void* x16,
                       int M, int N, int K, void* stream);
 
