@@ -895,7 +895,7 @@ def profile_kernels(torch, W, rank, world, barrier, steps=2):
     agg = collections.defaultdict(list)
     for e in prof.events():
         if e.device_type == torch.autograd.DeviceType.CUDA:
-            agg[e.name.split("(")[0][:100]].append(e.device_time_total)
+            agg[e.name.replace("(anonymous namespace)::", "").split("(")[0][:100]].append(e.device_time_total)
     rows = sorted(agg.items(), key=lambda kv: -sum(kv[1]))
     total = sum(sum(v) for _, v in rows) / steps
     text = "\n".join(f"kernels rank {rank}: {len(v) / steps:6.0f}/step {statistics.mean(v):9.2f} us  {k}"
