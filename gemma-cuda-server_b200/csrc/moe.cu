@@ -730,8 +730,10 @@ struct DownEpi {
     // DETERMINISTIC, rows to local memory: each lane converts its row's 32-column chunk to fp16 and stores it as four
     // 16-byte pieces (64 contiguous bytes of the row); no shared-memory transpose, so the epilogue's per-tile cost --
     // which bounds this short-K GEMM -- is a handful of instructions per chunk.
-    // DETERMINISTIC with `transpose`: each warp first transposes its 32 x 32 chunk through shared memory (32 x 33
-    // floats, the EPI_SMEM of DownTransposeCfg) and every store instruction writes four whole 64-byte row segments.
+    // DETERMINISTIC with `transpose`: each warp transposes its 32 x 32 chunk through shared memory as fp16, 16 rows
+    // at a time (16 x 17 words per warp, the EPI_SMEM of DownTransposeCfg: small enough to keep 4 pipeline stages;
+    // a 32 x 33 fp32 tile left room for 3 only, which cost the kernel 4-10 us), and every store instruction writes
+    // eight whole 64-byte row segments.
     // Used for rows to peer memory (16-byte pieces of 32 different rows per instruction cost NVLink packets of half a
     // 32-byte sector each) and for large row counts (the row buffer then streams to DRAM, where scattered 16-byte
     // pieces cost more than the transpose: 125 vs 105 us for 32768 rows of 2816).
@@ -748,25 +750,33 @@ struct DownEpi {
                 uint16_t* rowp = a < 0 ? nullptr
                                  : peer_back ? peer_back[a / capacity] + ((long long)rank * capacity + a % capacity) * H
                                              : y + (long long)a * H;
-                float* tile = reinterpret_cast<float*>(esm) + ((threadIdx.x >> 5) - 4) * (32 * 33);   // warps 4..
-                const int sub = lane >> 3, q = (lane & 7) * 4;
+                // per warp a 16-row x 17-word tile of fp16 pairs (the padding word spreads a column over the banks):
+                // the warp's 32 rows go through it in two halves of 16; in each of two rounds per half, lane
+                // (g, q) = (lane / 4, lane % 4) stores 16 bytes (columns 8q..8q+7) of row 8k + g of the half, so one
+                // store instruction writes whole 64-byte segments of 8 rows
+                uint32_t* tile = reinterpret_cast<uint32_t*>(esm) + ((threadIdx.x >> 5) - 4) * (16 * 17);   // warps 4..
+                const int g = lane >> 2, q = lane & 3;
 #pragma unroll
                 for (int c = 0; c < CH; ++c) {
                     const int n0 = ti.n0 + col_base + 32 * c;   // warp-uniform
                     if (n0 >= H) continue;
-                    __syncwarp();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) tile[lane * 33 + i] = s * __uint_as_float(r[c][i]);
-                    __syncwarp();
+                    for (int h = 0; h < 2; ++h) {
+                        __syncwarp();
+                        if ((lane >> 4) == h)
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        const int i = 4 * g + sub;
-                        uint16_t* pi = reinterpret_cast<uint16_t*>(
-                            __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), i));
-                        const float* src = tile + i * 33 + q;
-                        if (pi)
-                            *reinterpret_cast<uint2*>(pi + n0 + q) =
-                                make_uint2(pack_half2_sat(src[0], src[1]), pack_half2_sat(src[2], src[3]));
+                            for (int i = 0; i < 16; ++i)
+                                tile[(lane & 15) * 17 + i] = pack_half2_sat(s * __uint_as_float(r[c][2 * i]),
+                                                                            s * __uint_as_float(r[c][2 * i + 1]));
+                        __syncwarp();
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const int lr = 8 * k + g;
+                            uint16_t* pi = reinterpret_cast<uint16_t*>(__shfl_sync(
+                                0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), 16 * h + lr));
+                            const uint32_t* src = tile + lr * 17 + 4 * q;
+                            if (pi) *reinterpret_cast<uint4*>(pi + n0 + 8 * q) = make_uint4(src[0], src[1], src[2], src[3]);
+                        }
                     }
                 }
                 return;
@@ -1101,7 +1111,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint16_t* y_back,
 
 using GroupCfg = KCfg<256, 4, 1, 8>;
 using DownCfg = KCfg<256, 4, 1, 8>;   // K = I is short: the epilogue bounds it (direct fp16 row stores)
-using DownTransposeCfg = KCfg<256, 3, 1, 8, Kind::NVF4, 8 * 32 * 33 * 4>;   // + the epilogue's transpose tiles
+using DownTransposeCfg = KCfg<256, 4, 1, 8, Kind::NVF4, 8 * 16 * 17 * 4>;   // + the epilogue's transpose tiles
 constexpr int kDownTransposeRows = 16384;   // local row buffers at least this large take the transposed stores
 
 // ---------------------------------------------------------------------------------------------------------------
