@@ -40,6 +40,7 @@ import io
 import json
 import os
 import pathlib
+import re
 import statistics
 import subprocess
 import sys
@@ -895,7 +896,9 @@ def profile_kernels(torch, W, rank, world, barrier, steps=2):
     agg = collections.defaultdict(list)
     for e in prof.events():
         if e.device_type == torch.autograd.DeviceType.CUDA:
-            agg[e.name.replace("(anonymous namespace)::", "").split("(")[0][:100]].append(e.device_time_total)
+            name = e.name.replace("(anonymous namespace)::", "")
+            epi = re.search(r"(\w+Epi)\b", name)          # the GEMM core's instances differ by epilogue policy
+            agg[name.split("(")[0][:100] + (f" [{epi.group(1)}]" if epi else "")].append(e.device_time_total)
     rows = sorted(agg.items(), key=lambda kv: -sum(kv[1]))
     total = sum(sum(v) for _, v in rows) / steps
     text = "\n".join(f"kernels rank {rank}: {len(v) / steps:6.0f}/step {statistics.mean(v):9.2f} us  {k}"

@@ -756,6 +756,13 @@ struct DownEpi {
                 // store instruction writes whole 64-byte segments of 8 rows
                 uint32_t* tile = reinterpret_cast<uint32_t*>(esm) + ((threadIdx.x >> 5) - 4) * (16 * 17);   // warps 4..
                 const int g = lane >> 2, q = lane & 3;
+                uint16_t* prow[2][2];      // the row this lane stores in round k of half h (same for every chunk)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int k = 0; k < 2; ++k)
+                        prow[h][k] = reinterpret_cast<uint16_t*>(__shfl_sync(
+                            0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), 16 * h + 8 * k + g));
 #pragma unroll
                 for (int c = 0; c < CH; ++c) {
                     const int n0 = ti.n0 + col_base + 32 * c;   // warp-uniform
@@ -772,8 +779,7 @@ struct DownEpi {
 #pragma unroll
                         for (int k = 0; k < 2; ++k) {
                             const int lr = 8 * k + g;
-                            uint16_t* pi = reinterpret_cast<uint16_t*>(__shfl_sync(
-                                0xFFFFFFFFu, reinterpret_cast<unsigned long long>(rowp), 16 * h + lr));
+                            uint16_t* pi = prow[h][k];
                             const uint32_t* src = tile + lr * 17 + 4 * q;
                             if (pi) *reinterpret_cast<uint4*>(pi + n0 + 8 * q) = make_uint4(src[0], src[1], src[2], src[3]);
                         }
