@@ -382,10 +382,12 @@ int launch_w4a16_stream(float* out, const uint8_t* wp, const uint8_t* ws, float 
 // are loaded with the L2 evict-first priority (read once); the activations stay in L1/L2.
 template <int NT>
 struct W4T {
-    static constexpr int CW = NT == 1 ? 16 : 8;               // consumer warps (register budget of NT = 2)
+    // launched for one activation tile (M <= 8; the dispatch takes it for M <= 2): 16 consumer warps, 5 stages
+    static_assert(NT == 1, "one tile of 8 activation rows");
+    static constexpr int CW = 16;                              // consumer warps
     static constexpr int ROWS = 16 * CW;
     static constexpr int CODES = ROWS * 128, SCALES = ROWS * 16;
-    static constexpr int STAGES = NT == 1 ? 5 : 8;
+    static constexpr int STAGES = 5;
     static constexpr int THREADS = (CW + 1) * 32;
     static constexpr int SMEM = STAGES * (CODES + SCALES) + 2 * STAGES * 8 + 16 + 1024;
     static_assert(SMEM <= 232448, "shared memory");
