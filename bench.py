@@ -65,6 +65,8 @@ def parse_args():
     ap.add_argument("--workload", choices=["quant", "gemm", "moe", "ep", "w4a16", "linear"], default="ep")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ep-rows", type=int, default=512, help="ep: rows per step (512 = 32 sequences x 16 drafts)")
+    ap.add_argument("--ep-layers", type=int, default=30,
+                    help="ep: MoE layers in the stack (30 = cfg4; 1 keeps the device footprint small for ncu captures)")
     ap.add_argument("--ep-scaling", choices=["strong", "weak"], default="strong",
                     help="ep: strong = --ep-rows in total, split over the GPUs (the cfg4 contract); weak = --ep-rows "
                          "per GPU")
@@ -999,7 +1001,8 @@ def main():
         if args.ep_scaling == "strong" and args.ep_rows % world:
             raise SystemExit(f"--ep-rows {args.ep_rows} does not split over {world} GPUs")
         rows = args.ep_rows // world if args.ep_scaling == "strong" else args.ep_rows
-        W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange, T=rows, scaling=args.ep_scaling)
+        W = EpWorkload(pkg, torch, orc, rank=rank, world=world, exchange=exchange, T=rows, scaling=args.ep_scaling,
+                       L=args.ep_layers)
     else:
         W = {"quant": QuantWorkload, "gemm": GemmWorkload, "moe": MoeWorkload, "w4a16": W4a16Workload,
              "linear": LinearWorkload}[args.workload](pkg, torch, orc)
