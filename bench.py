@@ -54,7 +54,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # dram__bytes_read.sum + dram__bytes_write.sum (bytes) of the dominant kernel per launch, from the ncu captures
 # summarised under profiles/ (quantize_bf16_rows_kernel, nvf4_gemm_pair_kernel, the MoE gate/up GEMM).
 NCU_TRAFFIC = {"quant": 46.262272e6, "gemm": 335.105280e6, "moe": 366.175232e6,
-               "ep": 321.858304e6}   # ep: the layer's dominant kernel, the grouped gate/up GEMM (one launch)
+               "ep": 320.639744e6}   # ep: the layer's dominant kernel, the grouped gate/up GEMM (one launch)
 
 
 def parse_args():
